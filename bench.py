@@ -1,0 +1,448 @@
+#!/usr/bin/env python
+"""Benchmark: Gaussian-field delta-W render, forward + backward, whole SD1.5 UNet.
+
+Workload: the 128 attention-projection fields of an SD1.5
+UNet (widths 320/640/1280, cross-attention k/v 768 wide; 93,511,680 delta
+elements), K=256 Gaussians each with config 1's distributions, seeded synthetic
+parameters and upstream gradients (no dataset exists for this path).  One step =
+forward render of every field (bf16 delta, fp32 accumulation) + all-gather of
+the bf16 delta across ranks + backward (fp32 dL/d(delta) -> d_mu, d_chol_raw,
+d_amp).  Fields are partitioned across ranks by measured render cost; the total
+work is fixed as N grows (strong scaling).
+
+Metric: delta elements rendered forward+backward per second, whole job.
+value  -- device time of the step, inputs resident in HBM (CUDA events, max over ranks)
+e2e    -- the same step through the drop-in per-layer API (guass_b200.cuda_field),
+          with parameters and dL/d(delta) copied from pinned host memory and the
+          gradients copied back, every step
+cpu_baseline / --impl reference -- the CPU oracle (a C restatement of the
+          reference kernels, OpenMP over all host cores) on a bounded sample
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+       (N > 1 under torch.distributed.run; one process per GPU)
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import csv
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "Gaussian-field dW fwd+bwd elements/s (whole SD1.5 UNet, 128 projections, K=256)"
+UNIT = "elements/s"
+# FMA-pipe operations per (element, Gaussian) evaluation, per the survey's
+# roofline definition (forward ~9, backward ~25).
+OPS_PER_EVAL = {"render_fwd": 9, "render_bwd": 25}
+SM_FP32_LANES = 128
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    a = ap.parse_args()
+    a.warmup = max(3, a.warmup)
+    return a
+
+
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clock/throttle samples every 50 ms while running."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.t0 = self.t1 = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def mark(self, which):
+        setattr(self, which, time.time())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        rows = []
+        for rec in csv.reader(io.StringIO(out)):
+            if len(rec) < 10:
+                continue
+            try:
+                ts = time.mktime(time.strptime(rec[0].strip().split(".")[0], "%Y/%m/%d %H:%M:%S"))
+                rows.append((ts, [x.strip() for x in rec[1:]]))
+            except ValueError:
+                continue
+        lo, hi = (self.t0 or 0) - 1.0, (self.t1 or time.time()) + 1.0
+        win = [r for ts, r in rows if lo <= ts <= hi] or [r for _, r in rows]
+        sm = [float(r[1]) for r in win if r[1].replace(".", "", 1).isdigit()]
+        mx = [float(r[2]) for r in win if r[2].replace(".", "", 1).isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in win for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        loaded = [s for s in sm if mx and s > 0.5 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(win)}
+
+
+# ---------------------------------------------------------------------------
+def setup_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+class UNetWorkload:
+    """Fields of the whole UNet, partitioned; this rank's batch and buffers."""
+
+    def __init__(self, rank: int, world: int):
+        from guass_b200 import synthetic
+        from guass_b200.batched import FieldBatch, pack_fields
+        from guass_b200.partition import GatherLayout, field_costs, lpt_partition
+
+        self.rank, self.world = rank, world
+        self.fields = synthetic.cfg3()
+        shapes = [(f.out_features, f.in_features, f.k) for f in self.fields]
+        self.numels = [f.numel for f in self.fields]
+        self.total_elements = sum(self.numels)
+        # exact per-field cost from one binning pass over all fields
+        full = FieldBatch(shapes)
+        mu, chol, amp, _ = pack_fields(self.fields, device="cuda")
+        while full.ensure_capacity(mu, chol, amp):
+            pass
+        full.forward(mu, chol, amp)
+        tps = [full.tile_ptr_view(i).cpu() for i in range(len(shapes))]
+        self.costs = field_costs(tps, [(s[0], s[1]) for s in shapes])
+        self.total_evals = sum(self.costs)
+        self.total_pairs = full.total_pairs()
+        del full, mu, chol, amp
+        self.parts = lpt_partition(self.costs, world)
+        self.layout = GatherLayout(self.parts, self.numels)
+        self.gathered = torch.zeros(world, self.layout.slot, dtype=torch.bfloat16, device="cuda")
+        own = self.parts[rank]
+        self.own = own
+        own_fields = [self.fields[i] for i in own]
+        self.mu, self.chol, self.amp, self.grad = pack_fields(own_fields, device="cuda")
+        self.batch = FieldBatch([shapes[i] for i in own],
+                                delta_out=self.gathered[rank, :self.layout.rank_numel[rank]])
+        while self.batch.ensure_capacity(self.mu, self.chol, self.amp):
+            pass
+        assert self.batch.device_flags() == 0
+        self.own_evals = sum(self.costs[i] for i in own)
+
+    def step(self):
+        from guass_b200.partition import all_gather_slots
+
+        self.batch.forward(self.mu, self.chol, self.amp)
+        if self.world > 1:
+            all_gather_slots(self.gathered, self.rank)
+        self.batch.backward(self.grad, self.mu, self.chol, self.amp)
+
+
+def run_device_timed(w: UNetWorkload, steps: int, warmup: int, world: int):
+    from guass_b200 import _lib
+
+    L = _lib.lib()
+    for _ in range(warmup):
+        w.step()
+    torch.cuda.synchronize()
+    # 3 forward + 4 backward trace events per step (gfield.h, gf_trace_events)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(7 * steps)]
+    for e in evs:
+        e.record()
+    torch.cuda.synchronize()
+    handles = (ctypes.c_void_p * len(evs))(*[e.cuda_event for e in evs])
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    _lib.check(L.gf_trace_events(handles, len(evs)))
+    start.record()
+    for _ in range(steps):
+        w.step()
+    end.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    recorded = L.gf_trace_count()
+    _lib.check(L.gf_trace_events(None, 0))
+    assert recorded == len(evs), (recorded, len(evs))
+    ms = start.elapsed_time(end) / steps
+    names = ("bin", "render_fwd", None, "bwd_prep", "render_bwd", "bwd_finalize")
+    per = {n: [] for n in names if n}
+    for s in range(steps):
+        e = evs[7 * s: 7 * s + 7]
+        per["bin"].append(e[0].elapsed_time(e[1]))
+        per["render_fwd"].append(e[1].elapsed_time(e[2]))
+        per["bwd_prep"].append(e[3].elapsed_time(e[4]))
+        per["render_bwd"].append(e[4].elapsed_time(e[5]))
+        per["bwd_finalize"].append(e[5].elapsed_time(e[6]))
+        if world > 1:
+            per.setdefault("all_gather", []).append(e[2].elapsed_time(e[3]))
+    kern = {k: sum(v) / len(v) for k, v in per.items()}
+    return ms, kern
+
+
+def run_e2e(w: UNetWorkload, steps: int, warmup: int, world: int):
+    """The same step through the drop-in per-layer API with host buffers."""
+    from guass_b200 import cuda_field
+    from guass_b200.partition import all_gather_slots
+
+    ext = cuda_field.load_extension()
+    host = []
+    for i in w.own:
+        f = w.fields[i]
+        host.append(dict(mu=f.mu.pin_memory(), chol=f.chol_raw.pin_memory(), amp=f.amp.pin_memory(),
+                         grad=f.grad.pin_memory(), row=f.row_coords.cuda(), col=f.col_coords.cuda(),
+                         out=[torch.empty_like(f.mu).pin_memory(), torch.empty_like(f.chol_raw).pin_memory(),
+                              torch.empty_like(f.amp).pin_memory()]))
+    h2d = sum(sum(h[k].numel() * h[k].element_size() for k in ("mu", "chol", "amp", "grad")) for h in host)
+    d2h = sum(sum(o.numel() * o.element_size() for o in h["out"]) for h in host)
+
+    def step():
+        for i, h in zip(w.own, host):
+            mu = h["mu"].to("cuda", non_blocking=True)
+            chol = h["chol"].to("cuda", non_blocking=True)
+            amp = h["amp"].to("cuda", non_blocking=True)
+            delta, tp, ids = ext.gaussian_field_forward(h["row"], h["col"], mu, chol, amp, 32, 32, 3.0, False, 80.0)
+            w.layout.field_view(w.gathered, i).copy_(delta)  # the layer's bf16 weight dtype cast
+            g = h["grad"].to("cuda", non_blocking=True)
+            grads = ext.gaussian_field_backward(g, h["row"], h["col"], mu, chol, amp, tp, ids, 32, 32, 3.0, False,
+                                                80.0)
+            for o, gr in zip(h["out"], grads):
+                o.copy_(gr, non_blocking=True)
+        if world > 1:
+            all_gather_slots(w.gathered, w.rank)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end) / steps, world)
+    return ms, sum_over_ranks(h2d, world), sum_over_ranks(d2h, world)
+
+
+# ---------------------------------------------------------------------------
+def cpu_oracle_sample(fields, budget_s: float, order=None):
+    """Run the CPU oracle fwd+bwd over fields (in ``order``) until the time
+    budget is used (at least one field).  Returns (elements, seconds, names)."""
+    import oracle
+
+    order = order if order is not None else list(range(len(fields)))
+    done_el, done_t, names = 0, 0.0, []
+    for i in order:
+        f = fields[i]
+        t0 = time.perf_counter()
+        d, tp, ids = oracle.forward(f.row_coords, f.col_coords, f.mu, f.chol_raw, f.amp)
+        oracle.backward(f.grad, f.row_coords, f.col_coords, f.mu, f.chol_raw, f.amp, tp, ids)
+        done_t += time.perf_counter() - t0
+        done_el += f.numel
+        names.append(f.name)
+        if done_t >= budget_s:
+            break
+    return done_el, done_t, names
+
+
+def interleaved_order(n=128, stride=16):
+    return [i for s in range(stride) for i in range(s, n, stride)]
+
+
+def cpu_baseline(fields, budget_s):
+    import oracle
+
+    oracle.build()
+    threads = oracle.max_threads()
+    el, t, names = cpu_oracle_sample(fields, budget_s, interleaved_order(len(fields)))
+    return {"value": el / t, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{len(names)} of {len(fields)} fields ({el} elements, fwd+bwd) in {t:.2f} s, "
+                      f"OpenMP x{threads} threads, C restatement of the reference kernels (oracle/)"}
+
+
+def reference_arm(a, rank, world):
+    """--impl reference: the reference algorithm on the host cores (the CPU
+    oracle, since the reference's own CPU path is PyTorch code that cannot be
+    shipped to the GPU box), bounded samples per step."""
+    if rank != 0:
+        return
+    from guass_b200 import synthetic
+    import oracle
+
+    oracle.build()
+    fields = synthetic.cfg3()
+    order = interleaved_order(len(fields))
+    per_step = max(1, len(fields) // 16)
+    threads = oracle.max_threads()
+    for s in range(a.warmup):
+        sub = [order[(s * per_step + j) % len(order)] for j in range(per_step)]
+        cpu_oracle_sample(fields, 1e9, sub)
+    tot_el, tot_t = 0, 0.0
+    for s in range(a.steps):
+        sub = [order[(s * per_step + j) % len(order)] for j in range(per_step)]
+        el, t, _ = cpu_oracle_sample(fields, 1e9, sub)
+        tot_el += el
+        tot_t += t
+    value = tot_el / tot_t
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * tot_t / a.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE cfg3 shapes)",
+            "config": {"workload": "cfg3 whole-UNet, 128 projection fields, K=256", "sample_per_step":
+                       f"{per_step} of 128 fields, fwd+bwd", "elements_per_step_avg": tot_el / a.steps},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{per_step} fields per step x {a.steps} steps, OpenMP x{threads}"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+def load_traffic(kernel: str):
+    p = ROOT / "profiles" / f"{kernel}_unet_traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except ValueError:
+            return None
+    return None
+
+
+def main():
+    a = parse_args()
+    rank, world, local = setup_dist()
+    if a.impl == "reference":
+        reference_arm(a, rank, world)
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    w = UNetWorkload(rank, world)
+    sampler = ClockSampler() if local == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+        sampler.mark("t0")
+    ms_local, kern = run_device_timed(w, a.steps, a.warmup, world)
+    if sampler:
+        sampler.mark("t1")
+    ms = max_over_ranks(ms_local, world)
+    kern_max = {k: max_over_ranks(v, world) for k, v in kern.items()}
+    clocks = sampler.stop() if sampler else None
+    value = w.total_elements / (ms / 1e3)
+
+    e2e = None
+    if not a.no_e2e:
+        e2e_ms, h2d, d2h = run_e2e(w, max(3, min(a.steps, 10)), 2, world)
+        e2e = {"value": w.total_elements / (e2e_ms / 1e3), "unit": UNIT, "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "path": "guass_b200.cuda_field per-layer drop-in API, fp32 delta, pinned host params/grads"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cpu = cpu_baseline(w.fields, a.cpu_seconds)
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    # roofline of the dominant kernel (render_bwd): FMA-pipe ops per launch
+    sm_count = torch.cuda.get_device_properties(0).multi_processor_count
+    f_mhz = (clocks or {}).get("sm_mhz") or 1965.0
+    dom = max(("render_fwd", "render_bwd"), key=lambda k: kern_max[k])
+    evals = w.total_evals if world == 1 else max(
+        sum(w.costs[i] for i in p) for p in w.parts)  # the slowest rank's launch
+    achieved = evals * OPS_PER_EVAL[dom] / (kern_max[dom] / 1e3) / 1e12
+    peak = sm_count * SM_FP32_LANES * f_mhz * 1e6 / 1e12
+    traffic = load_traffic(dom)
+    bytes_step = w.total_elements * (2 + 4)  # bf16 delta written + fp32 dL/d(delta) read
+    with open(ROOT / "MEASURED_PEAKS.json") if (ROOT / "MEASURED_PEAKS.json").exists() else open(os.devnull) as fh:
+        txt = fh.read()
+    hbm_peak = json.loads(txt).get("hbm_gbs", 6650.0) if txt else 6650.0
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; BASELINE cfg3 shapes and cfg1 distributions)",
+        "config": {"workload": "cfg3 whole-UNet batched render, 128 projection fields, K=256",
+                   "elements": w.total_elements, "pairs": w.total_pairs, "evals": w.total_evals,
+                   "delta_dtype": "bf16", "grad_dtype": "f32", "tile": "32x32", "sigma_multiplier": 3.0,
+                   "clamp_quad": 80.0, "partition": f"LPT by render cost over {world} rank(s)",
+                   "parallelism": f"layer-partition x{world} + NCCL all-gather of bf16 delta" if world > 1
+                   else "single GPU",
+                   "l2": "no flush: each step writes 187 MB of delta and reads 374 MB of dL/d(delta) (> 126 MB L2)"},
+        "kernels_ms": kern_max,
+        "roofline": {"kernel": dom, "bound": "fp32", "achieved": achieved, "peak": peak, "unit": "Tops/s",
+                     "frac": achieved / peak,
+                     "traffic": (traffic or {}).get("bytes_per_launch"),
+                     "definition": f"{OPS_PER_EVAL[dom]} FMA-pipe ops x {evals} (element,Gaussian) evaluations "
+                                   f"per launch / CUDA-event launch time; peak = {sm_count} SMs x "
+                                   f"{SM_FP32_LANES} FP32 lanes x {f_mhz:.0f} MHz (sampled SM clock; "
+                                   "MEASURED_PEAKS.json has no FP32 figure)"},
+        "roofline_hbm": {"achieved": bytes_step / (ms / 1e3) / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": bytes_step / (ms / 1e3) / 1e9 / hbm_peak, "peak_source": "MEASURED_PEAKS.json hbm_gbs"},
+        "clocks": clocks,
+        "e2e": e2e,
+        "cpu_baseline": cpu,
+        "gpu_launches": 5 * a.steps * world,
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

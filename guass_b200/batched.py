@@ -1,0 +1,211 @@
+"""Batched all-layer renderer: every patched projection in one set of launches.
+
+The reference renders each ``GaussianLinear`` separately
+(gaussian_peft/layers/gaussian_linear.py:178-190), paying about 15 launches and
+one host sync per layer in the forward and about 40 launches and 6 syncs in the
+backward.  :class:`FieldBatch` renders a fixed set of fields (for example the
+128 attention projections of an SD1.5 UNet) with 2 forward and 3 backward
+launches in total and no host synchronisation.
+
+Packed layout (all on one device):
+  parameters  mu [sum K, 2], chol_raw [sum K, 3], amp [sum K, 1]   (field f at rows g_off[f]:)
+  outputs     delta [sum out*in] (bf16 by default)                  (field f at n_off[f]:)
+  binning     tile_ptr [sum (T+1)], ids [capacity], pair_base [n+1]
+  gradients   d_mu, d_chol_raw, d_amp with the parameters' layout
+The flat parameter/gradient layout is also what the data-parallel path
+all-reduces as one buffer.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from guass_b200 import _lib
+from guass_b200.cuda_field._ext import make_config
+
+_DT = {torch.float32: _lib.GF_F32, torch.bfloat16: _lib.GF_BF16}
+
+
+@dataclass(frozen=True)
+class FieldShape:
+    out_features: int
+    in_features: int
+    num_gaussians: int
+
+
+class FieldBatch:
+    """A fixed set of fields rendered together (at most GF_MAX_FIELDS)."""
+
+    def __init__(self, shapes, *, tile_out: int = 32, tile_in: int = 32, sigma_multiplier: float = 3.0,
+                 normalize: bool = False, clamp_quad: float | None = 80.0, out_dtype=torch.bfloat16,
+                 grad_dtype=torch.float32, out_scale: float = 1.0, device="cuda", ids_capacity: int | None = None,
+                 row_coords=None, col_coords=None, delta_out: torch.Tensor | None = None):
+        self.shapes = [s if isinstance(s, FieldShape) else FieldShape(*s) for s in shapes]
+        n = len(self.shapes)
+        if not 1 <= n <= _lib.GF_MAX_FIELDS:
+            raise ValueError(f"a batch holds 1..{_lib.GF_MAX_FIELDS} fields, got {n}")
+        dev = torch.device(device)
+        if dev.type == "cuda" and dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        self.device = dev
+        self.tile_out, self.tile_in = int(tile_out), int(tile_in)
+        self.out_dtype, self.grad_dtype = out_dtype, grad_dtype
+        self.cfg = make_config(tile_out, tile_in, sigma_multiplier, normalize, clamp_quad,
+                               out_dtype=_DT[out_dtype], grad_dtype=_DT[grad_dtype], out_scale=out_scale)
+        self._lib = _lib.lib()
+        L = self._lib
+        self.num_tiles = [int(L.gf_num_tiles(s.out_features, s.in_features, tile_out, tile_in)) for s in self.shapes]
+        self.g_off, self.n_off, self.t_off, self.r_off, self.c_off = [0], [0], [0], [0], [0]
+        for s, t in zip(self.shapes, self.num_tiles):
+            self.g_off.append(self.g_off[-1] + s.num_gaussians)
+            self.n_off.append(self.n_off[-1] + s.out_features * s.in_features)
+            self.t_off.append(self.t_off[-1] + t + 1)
+            self.r_off.append(self.r_off[-1] + s.out_features)
+            self.c_off.append(self.c_off[-1] + s.in_features)
+        dev = self.device
+        # axes: linspace(-1, 1) per field (gaussian_peft/kernels/coords.py:37-50) unless given
+        if row_coords is None:
+            row_coords = [torch.linspace(-1.0, 1.0, s.out_features, dtype=torch.float32) for s in self.shapes]
+        if col_coords is None:
+            col_coords = [torch.linspace(-1.0, 1.0, s.in_features, dtype=torch.float32) for s in self.shapes]
+        self.row = torch.cat([r.reshape(-1).float().cpu() for r in row_coords]).to(dev)
+        self.col = torch.cat([c.reshape(-1).float().cpu() for c in col_coords]).to(dev)
+        if delta_out is not None:
+            if delta_out.dtype != out_dtype or delta_out.numel() < self.n_off[-1] or not delta_out.is_contiguous():
+                raise ValueError(f"delta_out must be a contiguous {out_dtype} tensor of >= {self.n_off[-1]} elements")
+            self.delta = delta_out.view(-1)[:self.n_off[-1]]
+        else:
+            self.delta = torch.empty(self.n_off[-1], dtype=out_dtype, device=dev)
+        self.tile_ptr = torch.empty(self.t_off[-1], dtype=torch.int64, device=dev)
+        self.pair_base = torch.zeros(n + 1, dtype=torch.int64, device=dev)
+        total_g = self.g_off[-1]
+        cap = ids_capacity if ids_capacity is not None else 32 * total_g + 4096
+        self.ids = torch.empty(max(int(cap), 1), dtype=torch.int64, device=dev)
+        self.d_mu = torch.empty(total_g, 2, dtype=torch.float32, device=dev)
+        self.d_chol_raw = torch.empty(total_g, 3, dtype=torch.float32, device=dev)
+        self.d_amp = torch.empty(total_g, 1, dtype=torch.float32, device=dev)
+        self._ws = None
+        self._bound = None
+        self._grad_bound = None
+        self._fields = (_lib.GfField * n)()
+        self._batch = _lib.GfBatch(num_fields=n, fields=ctypes.cast(self._fields, ctypes.POINTER(_lib.GfField)))
+
+    # -- parameter helpers -------------------------------------------------
+    def num_fields(self) -> int:
+        return len(self.shapes)
+
+    def numel(self) -> int:
+        return self.n_off[-1]
+
+    def field_slice(self, f: int) -> slice:
+        return slice(self.g_off[f], self.g_off[f + 1])
+
+    def delta_view(self, f: int) -> torch.Tensor:
+        s = self.shapes[f]
+        return self.delta[self.n_off[f]:self.n_off[f + 1]].view(s.out_features, s.in_features)
+
+    def tile_ptr_view(self, f: int) -> torch.Tensor:
+        return self.tile_ptr[self.t_off[f]:self.t_off[f + 1]]
+
+    # -- binding -------------------------------------------------------------
+    def _bind_grad(self, grad):
+        if grad.dtype != self.grad_dtype or not grad.is_contiguous() or grad.numel() != self.numel() \
+                or grad.device != self.device:
+            raise RuntimeError(f"grad must be a contiguous {self.grad_dtype} tensor of {self.numel()} elements "
+                               f"on {self.device}")
+        if grad.data_ptr() == self._grad_bound:
+            return
+        esz = grad.element_size()
+        for f in range(len(self.shapes)):
+            self._fields[f].grad_delta = grad.data_ptr() + esz * self.n_off[f]
+        self._grad_bound = grad.data_ptr()
+
+    def _bind(self, mu, chol_raw, amp):
+        key = (mu.data_ptr(), chol_raw.data_ptr(), amp.data_ptr(), self.ids.data_ptr())
+        if key == self._bound:
+            return
+        total_g = self.g_off[-1]
+        for name, t, cols in (("mu", mu, 2), ("chol_raw", chol_raw, 3), ("amp", amp, 1)):
+            if t.dtype != torch.float32 or not t.is_contiguous() or t.device != self.device:
+                raise RuntimeError(f"{name} must be a contiguous float32 tensor on {self.device}")
+            if t.numel() != total_g * cols:
+                raise RuntimeError(f"{name} must have shape [{total_g}, {cols}]")
+        esz_out = self.delta.element_size()
+        for f, s in enumerate(self.shapes):
+            g0, n0 = self.g_off[f], self.n_off[f]
+            fd = self._fields[f]
+            fd.out_features, fd.in_features, fd.num_gaussians = s.out_features, s.in_features, s.num_gaussians
+            fd.row_coords = self.row.data_ptr() + 4 * self.r_off[f]
+            fd.col_coords = self.col.data_ptr() + 4 * self.c_off[f]
+            fd.mu = mu.data_ptr() + 8 * g0
+            fd.chol_raw = chol_raw.data_ptr() + 12 * g0
+            fd.amp = amp.data_ptr() + 4 * g0
+            fd.delta = self.delta.data_ptr() + esz_out * n0
+            fd.tile_ptr = self.tile_ptr.data_ptr() + 8 * self.t_off[f]
+            fd.gaussian_ids = None
+            fd.ids_capacity = 0
+            fd.d_mu = self.d_mu.data_ptr() + 8 * g0
+            fd.d_chol_raw = self.d_chol_raw.data_ptr() + 12 * g0
+            fd.d_amp = self.d_amp.data_ptr() + 4 * g0
+        self._batch.ids = self.ids.data_ptr()
+        self._batch.ids_capacity = self.ids.numel()
+        self._batch.pair_base = self.pair_base.data_ptr()
+        need = max(self._lib.gf_workspace_bytes(ctypes.byref(self.cfg), ctypes.byref(self._batch), p)
+                   for p in (_lib.GF_PASS_FORWARD, _lib.GF_PASS_BACKWARD))
+        if need == 0:
+            raise RuntimeError("invalid batch: " + _lib.last_error())
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        self._bound = key
+
+    # -- passes --------------------------------------------------------------
+    def forward(self, mu, chol_raw, amp, stream=None) -> torch.Tensor:
+        """Render every field into ``self.delta``; no host synchronisation."""
+        self._bind(mu, chol_raw, amp)
+        st = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        _lib.check(self._lib.gf_forward(ctypes.byref(self.cfg), ctypes.byref(self._batch), self._ws.data_ptr(),
+                                        self._ws.numel(), st))
+        return self.delta
+
+    def backward(self, grad, mu, chol_raw, amp, stream=None):
+        """dL/d(delta) (packed, grad_dtype) -> (d_mu, d_chol_raw, d_amp) packed."""
+        self._bind(mu, chol_raw, amp)
+        self._bind_grad(grad)
+        st = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        _lib.check(self._lib.gf_backward(ctypes.byref(self.cfg), ctypes.byref(self._batch), self._ws.data_ptr(),
+                                         self._ws.numel(), st))
+        return self.d_mu, self.d_chol_raw, self.d_amp
+
+    def device_flags(self, reset: bool = True) -> int:
+        """Synchronise and return the GF_FLAG_* bits recorded since the last reset."""
+        flags = ctypes.c_uint32(0)
+        _lib.check(self._lib.gf_workspace_status(self._ws.data_ptr(),
+                                                 torch.cuda.current_stream(self.device).cuda_stream,
+                                                 int(reset), ctypes.byref(flags)))
+        return flags.value
+
+    def total_pairs(self) -> int:
+        return int(self.pair_base[-1].item())
+
+    def ensure_capacity(self, mu, chol_raw, amp) -> bool:
+        """Run one forward, grow the id buffer if the pairs did not fit.
+        Returns True if it had to grow (the caller should render again)."""
+        self.forward(mu, chol_raw, amp)
+        flags = self.device_flags(reset=True)
+        p = self.total_pairs()
+        if p > self.ids.numel() or flags & _lib.GF_FLAG_CAPACITY:
+            self.ids = torch.empty(p + p // 8 + 1024, dtype=torch.int64, device=self.device)
+            self._bound = None
+            return True
+        return False
+
+
+def pack_fields(fields, device="cuda"):
+    """List of synthetic.FieldInputs -> packed (mu, chol_raw, amp, grad f32, row list, col list)."""
+    mu = torch.cat([f.mu for f in fields]).to(device).contiguous()
+    chol = torch.cat([f.chol_raw for f in fields]).to(device).contiguous()
+    amp = torch.cat([f.amp for f in fields]).to(device).contiguous()
+    grad = torch.cat([f.grad for f in fields]).to(device).contiguous()
+    return mu, chol, amp, grad

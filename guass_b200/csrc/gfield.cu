@@ -1,0 +1,1032 @@
+// gfield.cu -- B200 (sm_100a) Gaussian-field weight-delta renderer.
+//
+// Five kernels implement the whole path (forward: bin + render; backward:
+// prep + render + finalize), for one field or a batch of fields in the same
+// launches.  Layout and math are described per kernel below; the C ABI is in
+// include/gfield.h.
+//
+// Parity model.  The reference kernels (gaussian_peft/cuda_field/csrc/
+// forward.cu, backward.cu) are plain fp32 CUDA compiled with nvcc's default
+// contraction.  The parity-relevant arithmetic here (preprocess, quadratic
+// form, basis, accumulation) is written with explicit __f*_rn intrinsics so
+// that the operation sequence is fixed and equal to the one the reference
+// compiles to; the GPU parity tests check this bit-for-bit against the
+// reference's own extension.  expf/log1pf are CUDA's, as in the reference.
+// The library must be built WITHOUT --use_fast_math.
+
+#include "gfield.h"
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+namespace gf {
+
+// forward.cu:15-17
+constexpr float kCholEps = 1e-5f;
+constexpr float kCovFloor = 1e-8f;
+constexpr double kTwoPi = 6.28318530717958647692;
+
+constexpr int kBinThreads = 512;
+constexpr int kRenderThreads = 256;  // 8 warps; fast path tile = 32x32
+constexpr int kChunk = 256;          // candidate Gaussians tested per pass
+constexpr int kBinSmemCapInts = 24 * 1024;          // 96 KB diff array in smem
+constexpr int kBwdSmemCapFloats = 24 * 1024;        // 96 KB grad tile in smem
+
+struct Cfg {
+  int32_t tile_out, tile_in;
+  float sigma;      // (float)sigma_multiplier, as forward.cu:186
+  float nclamp;     // -0.5f * (float)clamp_quad (exact scaling)
+  float out_scale;
+  int32_t has_clamp, normalize;
+};
+
+// One field as the kernels see it (kernel-parameter space, read via LDC).
+struct DevField {
+  const float* row;
+  const float* col;
+  const float* mu;
+  const float* chol;
+  const float* amp;
+  void* delta;
+  int64_t* tile_ptr;
+  int64_t* ids;
+  const void* grad;
+  float* d_mu;
+  float* d_chol;
+  float* d_amp;
+  int64_t ids_cap;    // per-field id mode: capacity (fwd) / pair count (bwd)
+  int64_t part_base;  // per-field id mode: first partial slot of this field
+  int32_t out_f, in_f, K, ntr, ntc;
+  int32_t tile_base;  // first global tile index
+  int32_t g_base;     // first global Gaussian index
+  int32_t diff_base;  // first int of this field's global diff array
+  int32_t vec_ok;     // delta rows are 16-byte aligned for vector stores
+  int32_t pad_;
+};
+
+template <int NF>
+struct Params {
+  Cfg cfg;
+  int32_t n;
+  int32_t total_tiles;
+  int32_t total_g;
+  int32_t pad_;
+  uint32_t* status;
+  uint32_t* done;
+  float4* records;       // [total_g][2]
+  int4* boxes;           // [total_g]  (r0, r1, c0, c1)
+  int64_t* goff;         // [total_g]  first partial slot of each Gaussian
+  int64_t* field_pairs;  // [n]
+  int32_t* diff;         // global fallback for large tile grids
+  float4* partials;      // [part_cap][2]
+  int64_t part_cap;      // slots in partials (backward)
+  int64_t* batch_ids;    // shared-id mode or nullptr
+  int64_t batch_cap;
+  int64_t* pair_base;    // [n+1] (shared-id mode)
+  DevField f[NF];
+};
+
+// ---------------------------------------------------------------------------
+// Geometry (forward.cu:134-209), bit-exact.
+
+__device__ __forceinline__ float softplus_stable(float x) {
+  // forward.cu:25-27
+  return __fadd_rn(log1pf(expf(-fabsf(x))), fmaxf(x, 0.0f));
+}
+
+struct Geo {
+  float i00, i01, i11, det;  // inverse covariance (i10 == i01) and det
+  float l11, l21, l22;
+  int4 box;                  // tile_r0, tile_r1, tile_c0, tile_c1
+};
+
+__device__ __forceinline__ int64_t clamp64(int64_t v, int64_t lo, int64_t hi) {
+  return v < lo ? lo : (v > hi ? hi : v);
+}
+
+__device__ __forceinline__ Geo geometry(float mu_r, float mu_c, float raw11, float raw21,
+                                        float raw22, const DevField& F, const Cfg& c) {
+  Geo o;
+  o.l11 = __fadd_rn(softplus_stable(raw11), kCholEps);
+  o.l21 = raw21;
+  o.l22 = __fadd_rn(softplus_stable(raw22), kCholEps);
+  const float cov00 = __fmul_rn(o.l11, o.l11);
+  const float cov01 = __fmul_rn(o.l11, o.l21);
+  const float cov11 = __fmaf_rn(o.l21, o.l21, __fmul_rn(o.l22, o.l22));  // :170
+  o.det = fmaxf(__fmaf_rn(cov00, cov11, -__fmul_rn(cov01, cov01)), kCovFloor);  // :171
+  o.i00 = __fdiv_rn(cov11, o.det);
+  o.i01 = __fdiv_rn(-cov01, o.det);
+  o.i11 = __fdiv_rn(cov00, o.det);
+  const float std_r = __fsqrt_rn(fmaxf(cov00, kCovFloor));
+  const float std_c = __fsqrt_rn(fmaxf(cov11, kCovFloor));
+  const float rs = __fmul_rn(0.5f, (float)max(F.out_f - 1, 1));
+  const float cs = __fmul_rn(0.5f, (float)max(F.in_f - 1, 1));
+  const float ra = __fadd_rn(mu_r, 1.0f);
+  const float ca = __fadd_rn(mu_c, 1.0f);
+  const float rrad = __fmul_rn(__fmul_rn(c.sigma, std_r), rs);
+  const float crad = __fmul_rn(__fmul_rn(c.sigma, std_c), cs);
+  // :189-192; the centre product is fused into the +/- radius
+  int64_t rmin = __float2ll_rz(floorf(__fmaf_rn(ra, rs, -rrad)));
+  int64_t rmax = __float2ll_rz(ceilf(__fmaf_rn(ra, rs, rrad)));
+  int64_t cmin = __float2ll_rz(floorf(__fmaf_rn(ca, cs, -crad)));
+  int64_t cmax = __float2ll_rz(ceilf(__fmaf_rn(ca, cs, crad)));
+  rmin = clamp64(rmin, 0, F.out_f - 1);
+  rmax = clamp64(rmax, 0, F.out_f - 1);
+  cmin = clamp64(cmin, 0, F.in_f - 1);
+  cmax = clamp64(cmax, 0, F.in_f - 1);
+  o.box.x = (int)clamp64(rmin / c.tile_out, 0, F.ntr - 1);
+  o.box.y = (int)clamp64(rmax / c.tile_out, 0, F.ntr - 1);
+  o.box.z = (int)clamp64(cmin / c.tile_in, 0, F.ntc - 1);
+  o.box.w = (int)clamp64(cmax / c.tile_in, 0, F.ntc - 1);
+  return o;
+}
+
+// forward.cu:357-360: basis *= 1 / (2*pi*sqrt(max(det, floor)))
+__device__ __forceinline__ float norm_factor(float det) {
+  return __fdiv_rn(1.0f, __fmul_rn((float)kTwoPi, __fsqrt_rn(fmaxf(det, kCovFloor))));
+}
+
+// Render-side record of one Gaussian: two float4.
+//   a = (mu_row, mu_col, amp, norm_factor)
+//   b = (-0.5*i00, -0.5*i01, -0.5*i11, det)
+// Scaling the inverse by -0.5 is exact, so the quadratic form evaluated from
+// it is exactly -0.5*quad of the reference and expf() sees the same operand.
+__device__ __forceinline__ void store_record(float4* rec, float mu_r, float mu_c, float amp,
+                                             const Geo& g) {
+  rec[0] = make_float4(mu_r, mu_c, amp, norm_factor(g.det));
+  rec[1] = make_float4(-0.5f * g.i00, -0.5f * g.i01, -0.5f * g.i11, g.det);
+}
+
+// q' = -0.5 * dx^T A dx with the reference's association
+// (forward.cu:349-350: dx*(A00*dx + A01*dy) + dy*(A10*dx + A11*dy)).
+__device__ __forceinline__ float quad_scaled(float dx, float dy, float h00, float a01,
+                                            float h01, float a11) {
+  const float t1 = __fmaf_rn(h00, dx, a01);  // a01 = h01*dy
+  const float t2 = __fmaf_rn(h01, dx, a11);  // a11 = h11*dy
+  return __fmaf_rn(dx, t1, __fmul_rn(dy, t2));
+}
+
+template <int NF>
+__device__ __forceinline__ int field_of_tile(const Params<NF>& p, int t) {
+  int lo = 0, hi = p.n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.f[mid].tile_base <= t) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+template <int NF>
+__device__ __forceinline__ int field_of_gaussian(const Params<NF>& p, int g) {
+  int lo = 0, hi = p.n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.f[mid].g_base <= g) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// Block-wide exclusive scan of one int64 per thread (blockDim multiple of 32).
+__device__ __forceinline__ int64_t block_exclusive_scan(int64_t v, int64_t* s_warp, int64_t* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int64_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int64_t w = lane < nw ? s_warp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < nw) s_warp[lane] = w;  // inclusive warp prefix
+  }
+  __syncthreads();
+  const int64_t before = warp > 0 ? s_warp[warp - 1] : 0;
+  *total = s_warp[nw - 1];
+  __syncthreads();
+  return before + x - v;
+}
+
+// ---------------------------------------------------------------------------
+// Forward kernel 1: preprocess + stable binning, one CTA per field.
+//
+// Each Gaussian's tile box adds +1/-1 at its four corners of a
+// (ntr+1) x (ntc+1) difference array; a 2-D prefix sum gives every tile's
+// pair count, and an exclusive scan of the counts in row-major tile order
+// gives tile_ptr.  This replaces the reference's scan -> host sync -> pair
+// emission -> 64-bit radix sort -> atomic count -> scan chain
+// (forward.cu:428-511) with O(K + T) work and no host round trip.  In
+// shared-id mode the last CTA to finish turns the per-field pair counts into
+// pair_base.
+template <int NF>
+__global__ void __launch_bounds__(kBinThreads)
+bin_kernel(const __grid_constant__ Params<NF> p, int smem_cap_ints) {
+  extern __shared__ int s_dyn[];
+  __shared__ int64_t s_warp[32];
+  __shared__ int s_last;
+  const int fi = blockIdx.x;
+  const DevField& F = p.f[fi];
+  const int tid = threadIdx.x, bs = blockDim.x;
+  const int W = F.ntc + 1, H = F.ntr + 1, nd = H * W;
+  int* D = (nd <= smem_cap_ints) ? s_dyn : (p.diff + F.diff_base);
+  for (int i = tid; i < nd; i += bs) D[i] = 0;
+  __syncthreads();
+  for (int g = tid; g < F.K; g += bs) {
+    const float mu_r = F.mu[2 * g], mu_c = F.mu[2 * g + 1];
+    const Geo geo = geometry(mu_r, mu_c, F.chol[3 * g], F.chol[3 * g + 1], F.chol[3 * g + 2], F, p.cfg);
+    store_record(p.records + 2 * (size_t)(F.g_base + g), mu_r, mu_c, F.amp[g], geo);
+    p.boxes[F.g_base + g] = geo.box;
+    atomicAdd(&D[geo.box.x * W + geo.box.z], 1);
+    atomicAdd(&D[geo.box.x * W + geo.box.w + 1], -1);
+    atomicAdd(&D[(geo.box.y + 1) * W + geo.box.z], -1);
+    atomicAdd(&D[(geo.box.y + 1) * W + geo.box.w + 1], 1);
+  }
+  __syncthreads();
+  for (int r = tid; r < H; r += bs) {
+    int s = 0;
+    for (int c = 0; c < W; ++c) { s += D[r * W + c]; D[r * W + c] = s; }
+  }
+  __syncthreads();
+  for (int c = tid; c < W; c += bs) {
+    int s = 0;
+    for (int r = 0; r < H; ++r) { s += D[r * W + c]; D[r * W + c] = s; }
+  }
+  __syncthreads();
+  const int T = F.ntr * F.ntc;
+  const int per = (T + bs - 1) / bs;
+  const int t0 = min(T, tid * per), t1 = min(T, t0 + per);
+  int64_t local = 0;
+  for (int t = t0; t < t1; ++t) local += D[(t / F.ntc) * W + (t % F.ntc)];
+  int64_t total;
+  int64_t off = block_exclusive_scan(local, s_warp, &total);
+  for (int t = t0; t < t1; ++t) {
+    F.tile_ptr[t] = off;
+    off += D[(t / F.ntc) * W + (t % F.ntc)];
+  }
+  if (tid == 0) {
+    F.tile_ptr[T] = total;
+    p.field_pairs[fi] = total;
+    if (p.batch_ids == nullptr && total > F.ids_cap) atomicOr(p.status, GF_FLAG_CAPACITY);
+  }
+  if (p.batch_ids != nullptr) {
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = (atomicAdd(p.done, 1u) == gridDim.x - 1);
+    __syncthreads();
+    if (s_last && tid == 0) {
+      __threadfence();
+      int64_t acc = 0;
+      for (int i = 0; i < p.n; ++i) {
+        p.pair_base[i] = acc;
+        acc += *((volatile int64_t*)&p.field_pairs[i]);
+      }
+      p.pair_base[p.n] = acc;
+      if (acc > p.batch_cap) atomicOr(p.status, GF_FLAG_CAPACITY);
+      *p.done = 0u;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Forward kernel 2: tile render, one CTA (8 warps) per tile.
+//
+// Work is split into 32x32 sub-blocks (one for the default tile).  Lane =
+// column, warp w owns rows w, w+8, w+16, w+24, so the column offset dy and the
+// two products that depend on it are hoisted per Gaussian.  The tile's
+// Gaussian list is rebuilt here from the boxes: candidates are tested 256 at a
+// time and compacted with warp ballots, which keeps ascending id order, i.e.
+// exactly the reference's stable-sorted order (forward.cu:481-482).  The first
+// sub-block also writes the ids.  Each element sums amp*basis over that list
+// sequentially in fp32, as forward.cu:326-362 does, so fp32 output is
+// bit-identical.  Output goes through shared memory to 128-bit stores.
+template <int NF, bool NORM, bool CLAMP, int OUTT>
+__global__ void __launch_bounds__(kRenderThreads, 3)
+render_fwd_kernel(const __grid_constant__ Params<NF> p) {
+  __shared__ float4 s_rec[2 * kChunk];
+  __shared__ int s_list[kChunk];
+  __shared__ int s_wcnt[8];
+  __shared__ float s_out[32][33];
+  const int tg = blockIdx.x;
+  const int fi = field_of_tile(p, tg);
+  const DevField& F = p.f[fi];
+  const int t = tg - F.tile_base;
+  const int tr = t / F.ntc, tc = t % F.ntc;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row0 = tr * p.cfg.tile_out, col0 = tc * p.cfg.tile_in;
+  const int th = min(p.cfg.tile_out, F.out_f - row0);
+  const int tw = min(p.cfg.tile_in, F.in_f - col0);
+  const int64_t start = F.tile_ptr[t];
+  const int64_t count = F.tile_ptr[t + 1] - start;
+  int64_t* ids;
+  int64_t cap_left;
+  if (p.batch_ids != nullptr) {
+    const int64_t b = p.pair_base[fi];
+    ids = p.batch_ids + b + start;
+    cap_left = p.batch_cap - b - start;
+  } else {
+    ids = F.ids + start;
+    cap_left = F.ids_cap - start;
+  }
+  const float4* rec = p.records + 2 * (size_t)F.g_base;
+  const int4* box = p.boxes + F.g_base;
+  const float nclamp = p.cfg.nclamp;
+
+  for (int rb = 0; rb < th; rb += 32) {
+    for (int cb = 0; cb < tw; cb += 32) {
+      const bool first = (rb == 0 && cb == 0);
+      const int c = cb + lane;
+      const float cc = (c < tw) ? F.col[col0 + c] : 0.0f;
+      float cr[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int r = rb + warp + 8 * j;
+        cr[j] = (r < th) ? F.row[row0 + r] : 0.0f;
+      }
+      float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      int64_t found = 0;
+      for (int k0 = 0; k0 < F.K && found < count; k0 += kChunk) {
+        const int g = k0 + tid;
+        bool hit = false;
+        if (g < F.K) {
+          const int4 b = box[g];
+          hit = (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, hit);
+        if (lane == 0) s_wcnt[warp] = __popc(m);
+        __syncthreads();
+        int before = 0, total = 0;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          const int cw = s_wcnt[w];
+          before += (w < warp) ? cw : 0;
+          total += cw;
+        }
+        if (hit) {
+          const int pos = before + __popc(m & ((1u << lane) - 1u));
+          s_list[pos] = g;
+          if (first && found + pos < cap_left) ids[found + pos] = g;
+        }
+        __syncthreads();
+        if (tid < total) {
+          const int gg = s_list[tid];
+          s_rec[2 * tid] = rec[2 * gg];
+          s_rec[2 * tid + 1] = rec[2 * gg + 1];
+        }
+        __syncthreads();
+        for (int j = 0; j < total; ++j) {
+          const float4 a = s_rec[2 * j];
+          const float4 h = s_rec[2 * j + 1];
+          const float dy = __fsub_rn(cc, a.y);
+          const float a01 = __fmul_rn(h.y, dy);
+          const float a11 = __fmul_rn(h.z, dy);
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            const float dx = __fsub_rn(cr[jj], a.x);
+            float q = quad_scaled(dx, dy, h.x, a01, h.y, a11);
+            q = fminf(q, 0.0f);                 // quad = max(quad, 0)
+            if (CLAMP) q = fmaxf(q, nclamp);    // quad = min(quad, clamp)
+            float e = expf(q);
+            if (NORM) e = __fmul_rn(e, a.w);
+            v[jj] = __fmaf_rn(a.z, e, v[jj]);   // forward.cu:361
+          }
+        }
+        found += total;
+        __syncthreads();
+      }
+      if (first && tid == 0 && found != count) atomicOr(p.status, GF_FLAG_INTERNAL);
+
+      // Store the 32x32 sub-block.
+      const float sc = p.cfg.out_scale;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float val = v[j];
+        if (sc != 1.0f) val = __fmul_rn(val, sc);
+        s_out[warp + 8 * j][lane] = val;
+      }
+      __syncthreads();
+      const int bh = min(32, th - rb), bw = min(32, tw - cb);
+      const size_t base = (size_t)(row0 + rb) * F.in_f + (col0 + cb);
+      if (OUTT == GF_F32) {
+        float* out = reinterpret_cast<float*>(F.delta) + base;
+        const int r = tid >> 3, q4 = (tid & 7) * 4;
+        if (r < bh) {
+          if (F.vec_ok && q4 + 3 < bw) {
+            *reinterpret_cast<float4*>(out + (size_t)r * F.in_f + q4) =
+                make_float4(s_out[r][q4], s_out[r][q4 + 1], s_out[r][q4 + 2], s_out[r][q4 + 3]);
+          } else {
+            for (int k = 0; k < 4; ++k)
+              if (q4 + k < bw) out[(size_t)r * F.in_f + q4 + k] = s_out[r][q4 + k];
+          }
+        }
+      } else {
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(F.delta) + base;
+        if (tid < 128) {
+          const int r = tid >> 2, q8 = (tid & 3) * 8;
+          if (r < bh) {
+            if (F.vec_ok && q8 + 7 < bw) {
+              uint32_t w[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const __nv_bfloat162 h2 = __floats2bfloat162_rn(s_out[r][q8 + 2 * k], s_out[r][q8 + 2 * k + 1]);
+                w[k] = *reinterpret_cast<const uint32_t*>(&h2);
+              }
+              *reinterpret_cast<uint4*>(out + (size_t)r * F.in_f + q8) = make_uint4(w[0], w[1], w[2], w[3]);
+            } else {
+              for (int k = 0; k < 8; ++k)
+                if (q8 + k < bw) out[(size_t)r * F.in_f + q8 + k] = __float2bfloat16_rn(s_out[r][q8 + k]);
+            }
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Backward kernel 1: per-field preprocess (backward.cu:552-557 rebuilds the
+// geometry too), plus each Gaussian's first slot in the pair-partial buffer:
+// an exclusive scan of tiles_touched, i.e. the reference's pair emission
+// order (forward.cu:211-241).  Also checks that the saved pair count matches.
+template <int NF>
+__global__ void __launch_bounds__(kBinThreads)
+bwd_prep_kernel(const __grid_constant__ Params<NF> p) {
+  __shared__ int64_t s_warp[32];
+  const int fi = blockIdx.x;
+  const DevField& F = p.f[fi];
+  const int tid = threadIdx.x, bs = blockDim.x;
+  const int per = (F.K + bs - 1) / bs;
+  const int g0 = min(F.K, tid * per), g1 = min(F.K, g0 + per);
+  int64_t local = 0;
+  for (int g = g0; g < g1; ++g) {
+    const float mu_r = F.mu[2 * g], mu_c = F.mu[2 * g + 1];
+    const Geo geo = geometry(mu_r, mu_c, F.chol[3 * g], F.chol[3 * g + 1], F.chol[3 * g + 2], F, p.cfg);
+    store_record(p.records + 2 * (size_t)(F.g_base + g), mu_r, mu_c, F.amp[g], geo);
+    p.boxes[F.g_base + g] = geo.box;
+    local += (int64_t)(geo.box.y - geo.box.x + 1) * (geo.box.w - geo.box.z + 1);
+  }
+  int64_t total;
+  int64_t off = block_exclusive_scan(local, s_warp, &total);
+  int64_t base, npairs;
+  if (p.batch_ids != nullptr) {
+    base = p.pair_base[fi];
+    npairs = p.pair_base[fi + 1] - base;
+  } else {
+    base = F.part_base;
+    npairs = F.ids_cap;
+  }
+  for (int g = g0; g < g1; ++g) {
+    p.goff[F.g_base + g] = base + off;
+    const int4 b = p.boxes[F.g_base + g];
+    off += (int64_t)(b.y - b.x + 1) * (b.w - b.z + 1);
+  }
+  if (tid == 0) {
+    const int64_t T = (int64_t)F.ntr * F.ntc;
+    if (total != npairs || F.tile_ptr[T] != npairs || F.tile_ptr[0] != 0)
+      atomicOr(p.status, GF_FLAG_STATE);
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+template <int GT>
+__device__ __forceinline__ float load_grad(const void* g, size_t i) {
+  if (GT == GF_F32) return reinterpret_cast<const float*>(g)[i];
+  return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(g)[i]);
+}
+
+// ---------------------------------------------------------------------------
+// Backward kernel 2: per-pair partial gradients, one CTA (8 warps) per tile.
+//
+// The tile's dL/d(delta) is read from HBM once into shared memory (the
+// reference re-reads it once per pair, backward.cu:301-308).  Warp i handles
+// the tile's pairs i, i+8, ...; lane = column, so dy is fixed per lane and the
+// per-element work is the basis plus four running sums:
+//   T0 = sum g*b,  U0 = sum g*b*[q active],  U1 = sum .. *dx,  U2 = sum .. *dx^2
+// from which the reference's per-pair channels follow exactly in real
+// arithmetic (backward.cu:330-351, with A01 == A10):
+//   amp: T0                  mu0: A00*U1 + A01*dy*U0   mu1: A01*U1 + A11*dy*U0
+//   A00: U2   A01 = A10: dy*U1   A11: dy^2*U0      (times amp, -0.5 later)
+// Lanes are reduced with a fixed xor-shuffle tree and lane 0 writes the six
+// channels to the pair's slot, goff[g] + (its tile's index in g's box), so the
+// finalize kernel reads each Gaussian's pairs contiguously.
+// Saved-state checks: id in range, strictly ascending inside the tile, tile
+// inside the Gaussian's box; a failing pair sets GF_FLAG_STATE and is skipped.
+template <int NF, bool NORM, bool CLAMP, int GT>
+__global__ void __launch_bounds__(kRenderThreads)
+render_bwd_kernel(const __grid_constant__ Params<NF> p) {
+  extern __shared__ float s_g[];  // [tile_out][tile_in] then [tile_out] row coords
+  const int tg = blockIdx.x;
+  const int fi = field_of_tile(p, tg);
+  const DevField& F = p.f[fi];
+  const int t = tg - F.tile_base;
+  const int tr = t / F.ntc, tc = t % F.ntc;
+  const int64_t start = F.tile_ptr[t];
+  const int64_t count = F.tile_ptr[t + 1] - start;
+  if (count <= 0) return;
+  // The saved binning is caller data: never index outside the id buffer.
+  const int64_t id_base = (p.batch_ids != nullptr) ? p.pair_base[fi] : 0;
+  const int64_t id_limit = (p.batch_ids != nullptr) ? p.batch_cap : F.ids_cap;
+  if (start < 0 || id_base < 0 || id_base + start + count > id_limit) {
+    if (threadIdx.x == 0) atomicOr(p.status, GF_FLAG_STATE);
+    return;
+  }
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int TO = p.cfg.tile_out, TI = p.cfg.tile_in;
+  const int row0 = tr * TO, col0 = tc * TI;
+  const int th = min(TO, F.out_f - row0), tw = min(TI, F.in_f - col0);
+  float* s_row = s_g + TO * TI;
+  for (int e = tid; e < TO * TI; e += blockDim.x) {
+    const int r = e / TI, c = e - r * TI;
+    s_g[e] = (r < th && c < tw) ? load_grad<GT>(F.grad, (size_t)(row0 + r) * F.in_f + col0 + c) : 0.0f;
+  }
+  for (int r = tid; r < TO; r += blockDim.x) s_row[r] = (r < th) ? F.row[row0 + r] : 0.0f;
+  __syncthreads();
+  const int64_t* ids = ((p.batch_ids != nullptr) ? p.batch_ids : F.ids) + id_base + start;
+  const float4* rec = p.records + 2 * (size_t)F.g_base;
+  const int4* box = p.boxes + F.g_base;
+  const float nclamp = p.cfg.nclamp;
+
+  for (int64_t i = warp; i < count; i += 8) {
+    const int64_t gid = ids[i];
+    bool ok = (gid >= 0) && (gid < F.K);
+    if (ok && i > 0) ok = ids[i - 1] < gid;
+    int4 b = make_int4(0, -1, 0, -1);
+    if (ok) {
+      b = box[gid];
+      ok = (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
+    }
+    if (!ok) {
+      if (lane == 0) atomicOr(p.status, GF_FLAG_STATE);
+      continue;
+    }
+    const float4 a = rec[2 * gid];
+    const float4 h = rec[2 * gid + 1];
+    float ch[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int cb = 0; cb < tw; cb += 32) {
+      const int c = cb + lane;
+      const bool cval = c < tw;
+      const float cc = cval ? F.col[col0 + c] : 0.0f;
+      const float dy = cval ? __fsub_rn(cc, a.y) : 0.0f;
+      const float a01 = __fmul_rn(h.y, dy);
+      const float a11 = __fmul_rn(h.z, dy);
+      float T0 = 0.f, U0 = 0.f, U1 = 0.f, U2 = 0.f;
+      const float* gcol = s_g + (cval ? c : 0);
+      for (int r = 0; r < th; ++r) {
+        const float dx = __fsub_rn(s_row[r], a.x);
+        float q = quad_scaled(dx, dy, h.x, a01, h.y, a11);
+        q = fminf(q, 0.0f);
+        bool act = true;
+        if (CLAMP) {
+          act = q > nclamp;          // reference: quad < clamp
+          q = fmaxf(q, nclamp);
+        }
+        float e = expf(q);
+        if (NORM) e = __fmul_rn(e, a.w);
+        const float gb = (cval ? gcol[r * TI] : 0.0f) * e;
+        T0 += gb;
+        const float gba = act ? gb : 0.0f;
+        U0 += gba;
+        U1 = fmaf(gba, dx, U1);
+        U2 = fmaf(gba * dx, dx, U2);
+      }
+      const float i00 = -2.0f * h.x, i01 = -2.0f * h.y, i11 = -2.0f * h.z;
+      const float dyU0 = dy * U0;
+      ch[0] += T0;
+      ch[1] += i00 * U1 + i01 * dyU0;
+      ch[2] += i01 * U1 + i11 * dyU0;
+      ch[3] += U2;
+      ch[4] += dy * U1;
+      ch[5] += dy * dyU0;
+    }
+#pragma unroll
+    for (int k = 0; k < 6; ++k) ch[k] = warp_sum(ch[k]);
+    if (lane == 0) {
+      const int64_t slot = p.goff[F.g_base + gid] + (int64_t)(tr - b.x) * (b.w - b.z + 1) + (tc - b.z);
+      if (slot >= 0 && slot < p.part_cap) {
+        p.partials[2 * slot] = make_float4(ch[0], ch[1], ch[2], ch[3]);
+        p.partials[2 * slot + 1] = make_float4(ch[4], ch[5], 0.0f, 0.0f);
+      } else {
+        atomicOr(p.status, GF_FLAG_STATE);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Backward kernel 3: one warp per Gaussian.  Sums the Gaussian's pair
+// partials (contiguous, fixed order) in fp64, applies amp and -0.5, and
+// evaluates the covariance chain of backward.cu:436-496 in fp64 before the
+// final fp32 store.  The chain dSigma = -A G A cancels strongly for
+// elongated Gaussians (|A| up to ~1e5); in fp32 that cancellation costs up to
+// ~1e-4 of the result, in fp64 nothing measurable.  Per Gaussian this is a
+// few dozen fp64 operations.
+template <int NF, bool NORM>
+__global__ void __launch_bounds__(kRenderThreads)
+bwd_finalize_kernel(const __grid_constant__ Params<NF> p) {
+  const int lane = threadIdx.x & 31;
+  const int G = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (G >= p.total_g) return;
+  const int fi = field_of_gaussian(p, G);
+  const DevField& F = p.f[fi];
+  const int g = G - F.g_base;
+  const int4 b = p.boxes[G];
+  const int64_t n = (int64_t)(b.y - b.x + 1) * (b.w - b.z + 1);
+  const int64_t o = p.goff[G];
+  double s[6] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0};
+  const int64_t jn = (o >= 0 && o + n <= p.part_cap) ? n : 0;  // inconsistent state was flagged already
+  for (int64_t j = lane; j < jn; j += 32) {
+    const float4 x = p.partials[2 * (o + j)];
+    const float4 y = p.partials[2 * (o + j) + 1];
+    s[0] += x.x; s[1] += x.y; s[2] += x.z; s[3] += x.w; s[4] += y.x; s[5] += y.y;
+  }
+#pragma unroll
+  for (int k = 0; k < 6; ++k) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s[k] += __shfl_xor_sync(0xffffffffu, s[k], off);
+  }
+  if (lane != 0) return;
+  const float mu_r = F.mu[2 * g], mu_c = F.mu[2 * g + 1];
+  const float raw11 = F.chol[3 * g], raw21 = F.chol[3 * g + 1], raw22 = F.chol[3 * g + 2];
+  const Geo geo = geometry(mu_r, mu_c, raw11, raw21, raw22, F, p.cfg);
+  const double amp = F.amp[g];
+  F.d_amp[g] = (float)s[0];
+  F.d_mu[2 * g] = (float)(amp * s[1]);
+  F.d_mu[2 * g + 1] = (float)(amp * s[2]);
+  const double m = -0.5 * amp;
+  const double g00 = m * s[3], g01 = m * s[4], g10 = g01, g11 = m * s[5];
+  const double det = geo.det;
+  double gdet = 0.0;
+  if (NORM) gdet = amp * (-0.5 / (double)fmaxf(geo.det, kCovFloor)) * s[0];
+  // backward.cu:469-495 with A^T = A (A01 == A10)
+  const double a00 = geo.i00, a01 = geo.i01, a11 = geo.i11;
+  const double b00 = g00 * a00 + g01 * a01;
+  const double b01 = g00 * a01 + g01 * a11;
+  const double b10 = g10 * a00 + g11 * a01;
+  const double b11 = g10 * a01 + g11 * a11;
+  const double c00 = -(a00 * b00 + a01 * b10) + gdet * det * a00;
+  const double c01 = -(a00 * b01 + a01 * b11) + gdet * det * a01;
+  const double c10 = -(a01 * b00 + a11 * b10) + gdet * det * a01;
+  const double c11 = -(a01 * b01 + a11 * b11) + gdet * det * a11;
+  const double l11 = geo.l11, l21 = geo.l21, l22 = geo.l22;
+  const double d_l11 = c00 * (2.0 * l11) + c01 * l21 + c10 * l21;
+  const double d_l21 = c01 * l11 + c10 * l11 + c11 * (2.0 * l21);
+  const double d_l22 = c11 * (2.0 * l22);
+  const double sg11 = 1.0 / (1.0 + exp(-(double)raw11));
+  const double sg22 = 1.0 / (1.0 + exp(-(double)raw22));
+  F.d_chol[3 * g] = (float)(d_l11 * sg11);
+  F.d_chol[3 * g + 1] = (float)d_l21;
+  F.d_chol[3 * g + 2] = (float)(d_l22 * sg22);
+}
+
+// ---------------------------------------------------------------------------
+// Host side.
+
+thread_local std::string g_last_error;
+
+struct Trace {
+  void* const* ev = nullptr;
+  int n = 0;
+  int used = 0;
+};
+thread_local Trace g_trace;
+
+inline void trace_mark(cudaStream_t st) {
+  if (g_trace.used < g_trace.n) {
+    cudaEventRecord(reinterpret_cast<cudaEvent_t>(g_trace.ev[g_trace.used]), st);
+    ++g_trace.used;
+  }
+}
+
+gf_status fail(gf_status s, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+gf_status fail(gf_status s, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return s;
+}
+
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct Layout {
+  size_t hdr, records, boxes, goff, field_pairs, diff, partials, total;
+  int64_t total_tiles, total_g, diff_ints, pair_cap;
+};
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+gf_status validate(const gf_config* cfg, const gf_batch* batch, gf_pass pass, bool data = true) {
+  if (!cfg || !batch) return fail(GF_ERR_INVALID_ARG, "cfg and batch must be non-null");
+  if (cfg->tile_out <= 0) return fail(GF_ERR_INVALID_ARG, "tile_out must be positive");
+  if (cfg->tile_in <= 0) return fail(GF_ERR_INVALID_ARG, "tile_in must be positive");
+  if (!(cfg->sigma_multiplier > 0.0)) return fail(GF_ERR_INVALID_ARG, "sigma_multiplier must be positive");
+  if (cfg->out_dtype != GF_F32 && cfg->out_dtype != GF_BF16) return fail(GF_ERR_INVALID_ARG, "out_dtype must be GF_F32 or GF_BF16");
+  if (cfg->grad_dtype != GF_F32 && cfg->grad_dtype != GF_BF16) return fail(GF_ERR_INVALID_ARG, "grad_dtype must be GF_F32 or GF_BF16");
+  if (batch->num_fields < 1 || batch->num_fields > GF_MAX_FIELDS)
+    return fail(GF_ERR_INVALID_ARG, "num_fields must be in [1, %d], got %d", GF_MAX_FIELDS, batch->num_fields);
+  if (!batch->fields) return fail(GF_ERR_INVALID_ARG, "fields must be non-null");
+  if (batch->ids && !batch->pair_base) return fail(GF_ERR_INVALID_ARG, "pair_base is required with a shared ids buffer");
+  if (pass == GF_PASS_BACKWARD && (int64_t)cfg->tile_out * cfg->tile_in > kBwdSmemCapFloats - cfg->tile_out)
+    return fail(GF_ERR_UNSUPPORTED, "tile_out*tile_in too large for the backward shared-memory tile");
+  int64_t tiles = 0, gs = 0;
+  for (int i = 0; i < batch->num_fields; ++i) {
+    const gf_field& f = batch->fields[i];
+    if (f.out_features <= 0 || f.in_features <= 0)
+      return fail(GF_ERR_INVALID_ARG, "field %d: out_features and in_features must be positive", i);
+    if (f.num_gaussians < 0) return fail(GF_ERR_INVALID_ARG, "field %d: num_gaussians must be >= 0", i);
+    if (f.out_features > INT32_MAX / 2 || f.in_features > INT32_MAX / 2 || f.num_gaussians > INT32_MAX / 2)
+      return fail(GF_ERR_UNSUPPORTED, "field %d: dimensions exceed the 32-bit index envelope", i);
+    if (!data) {
+      tiles += ceil_div(f.out_features, cfg->tile_out) * ceil_div(f.in_features, cfg->tile_in);
+      gs += f.num_gaussians;
+      continue;
+    }
+    if (!f.row_coords || !f.col_coords || !f.tile_ptr)
+      return fail(GF_ERR_INVALID_ARG, "field %d: row_coords, col_coords and tile_ptr must be non-null", i);
+    if (f.num_gaussians > 0 && (!f.mu || !f.chol_raw || !f.amp))
+      return fail(GF_ERR_INVALID_ARG, "field %d: mu, chol_raw and amp must be non-null", i);
+    if (!batch->ids && f.ids_capacity > 0 && !f.gaussian_ids)
+      return fail(GF_ERR_INVALID_ARG, "field %d: gaussian_ids must be non-null", i);
+    if (!batch->ids && f.ids_capacity < 0) return fail(GF_ERR_INVALID_ARG, "field %d: ids_capacity must be >= 0", i);
+    if (pass == GF_PASS_FORWARD && !f.delta) return fail(GF_ERR_INVALID_ARG, "field %d: delta must be non-null", i);
+    if (pass == GF_PASS_BACKWARD) {
+      if (!f.grad_delta) return fail(GF_ERR_INVALID_ARG, "field %d: grad_delta must be non-null", i);
+      if (f.num_gaussians > 0 && (!f.d_mu || !f.d_chol_raw || !f.d_amp))
+        return fail(GF_ERR_INVALID_ARG, "field %d: d_mu, d_chol_raw and d_amp must be non-null", i);
+    }
+    tiles += ceil_div(f.out_features, cfg->tile_out) * ceil_div(f.in_features, cfg->tile_in);
+    gs += f.num_gaussians;
+  }
+  if (tiles > INT32_MAX / 2 || gs > INT32_MAX / 2) return fail(GF_ERR_UNSUPPORTED, "batch exceeds the 32-bit index envelope");
+  return GF_OK;
+}
+
+Layout layout(const gf_config* cfg, const gf_batch* batch, gf_pass pass) {
+  Layout L{};
+  for (int i = 0; i < batch->num_fields; ++i) {
+    const gf_field& f = batch->fields[i];
+    const int64_t ntr = ceil_div(f.out_features, cfg->tile_out), ntc = ceil_div(f.in_features, cfg->tile_in);
+    L.total_tiles += ntr * ntc;
+    L.total_g += f.num_gaussians;
+    const int64_t nd = (ntr + 1) * (ntc + 1);
+    if (nd > kBinSmemCapInts) L.diff_ints += nd;
+    if (!batch->ids) L.pair_cap += f.ids_capacity;
+  }
+  if (batch->ids) L.pair_cap = batch->ids_capacity;
+  size_t off = 0;
+  L.hdr = off; off += 256;
+  L.records = off; off = align256(off + 32 * (size_t)L.total_g);
+  L.boxes = off; off = align256(off + 16 * (size_t)L.total_g);
+  L.goff = off; off = align256(off + 8 * (size_t)L.total_g);
+  L.field_pairs = off; off = align256(off + 8 * (size_t)batch->num_fields);
+  L.diff = off; off = align256(off + 4 * (size_t)L.diff_ints);
+  L.partials = off;
+  if (pass == GF_PASS_BACKWARD) off = align256(off + 32 * (size_t)L.pair_cap);
+  L.total = off;
+  return L;
+}
+
+template <int NF>
+void fill_params(Params<NF>& P, const gf_config* cfg, const gf_batch* batch, const Layout& L, char* ws) {
+  memset(&P, 0, sizeof(P));
+  P.cfg.tile_out = (int32_t)cfg->tile_out;
+  P.cfg.tile_in = (int32_t)cfg->tile_in;
+  P.cfg.sigma = (float)cfg->sigma_multiplier;
+  P.cfg.nclamp = -0.5f * (float)cfg->clamp_quad;
+  P.cfg.out_scale = cfg->out_scale;
+  P.cfg.has_clamp = cfg->has_clamp_quad != 0;
+  P.cfg.normalize = cfg->normalize != 0;
+  P.n = batch->num_fields;
+  P.total_tiles = (int32_t)L.total_tiles;
+  P.total_g = (int32_t)L.total_g;
+  P.status = reinterpret_cast<uint32_t*>(ws + L.hdr);
+  P.done = reinterpret_cast<uint32_t*>(ws + L.hdr + 4);
+  P.records = reinterpret_cast<float4*>(ws + L.records);
+  P.boxes = reinterpret_cast<int4*>(ws + L.boxes);
+  P.goff = reinterpret_cast<int64_t*>(ws + L.goff);
+  P.field_pairs = reinterpret_cast<int64_t*>(ws + L.field_pairs);
+  P.diff = reinterpret_cast<int32_t*>(ws + L.diff);
+  P.partials = reinterpret_cast<float4*>(ws + L.partials);
+  P.part_cap = L.pair_cap;
+  P.batch_ids = batch->ids;
+  P.batch_cap = batch->ids_capacity;
+  P.pair_base = batch->pair_base;
+  int32_t tile_base = 0, g_base = 0, diff_base = 0;
+  int64_t part_base = 0;
+  const size_t esz = cfg->out_dtype == GF_BF16 ? 2 : 4;
+  for (int i = 0; i < batch->num_fields; ++i) {
+    const gf_field& s = batch->fields[i];
+    DevField& d = P.f[i];
+    d.row = s.row_coords; d.col = s.col_coords; d.mu = s.mu; d.chol = s.chol_raw; d.amp = s.amp;
+    d.delta = s.delta; d.tile_ptr = s.tile_ptr; d.ids = s.gaussian_ids; d.grad = s.grad_delta;
+    d.d_mu = s.d_mu; d.d_chol = s.d_chol_raw; d.d_amp = s.d_amp;
+    d.ids_cap = s.ids_capacity;
+    d.part_base = part_base;
+    if (!batch->ids) part_base += s.ids_capacity;
+    d.out_f = (int32_t)s.out_features;
+    d.in_f = (int32_t)s.in_features;
+    d.K = (int32_t)s.num_gaussians;
+    d.ntr = (int32_t)ceil_div(s.out_features, cfg->tile_out);
+    d.ntc = (int32_t)ceil_div(s.in_features, cfg->tile_in);
+    d.tile_base = tile_base;
+    d.g_base = g_base;
+    const int32_t nd = (d.ntr + 1) * (d.ntc + 1);
+    d.diff_base = diff_base;
+    if (nd > kBinSmemCapInts) diff_base += nd;
+    tile_base += d.ntr * d.ntc;
+    g_base += d.K;
+    const size_t vec = 16 / esz;
+    d.vec_ok = ((reinterpret_cast<uintptr_t>(s.delta) & 15u) == 0) && (s.in_features % (int64_t)vec == 0) &&
+               (cfg->tile_in % (int64_t)vec == 0);
+  }
+}
+
+#define GF_LAUNCH_CHECK(what)                                                         \
+  do {                                                                                \
+    cudaError_t e_ = cudaGetLastError();                                              \
+    if (e_ != cudaSuccess) return fail(GF_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e_)); \
+  } while (0)
+
+template <int NF>
+gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout& L, char* ws, cudaStream_t st) {
+  // The descriptor block is large; keep one per thread instead of on the stack.
+  thread_local Params<NF>* tp = nullptr;
+  if (!tp) tp = new Params<NF>();
+  Params<NF>& p = *tp;
+  fill_params(p, cfg, batch, L, ws);
+  int max_nd = 0;
+  for (int i = 0; i < p.n; ++i) {
+    const int nd = (p.f[i].ntr + 1) * (p.f[i].ntc + 1);
+    if (nd <= kBinSmemCapInts && nd > max_nd) max_nd = nd;
+  }
+  const size_t smem = sizeof(int) * (size_t)max_nd;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(bin_kernel<NF>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBinSmemCapInts * 4);
+    attr_set = true;
+  }
+  trace_mark(st);
+  bin_kernel<NF><<<p.n, kBinThreads, smem, st>>>(p, kBinSmemCapInts);
+  GF_LAUNCH_CHECK("bin_kernel");
+  trace_mark(st);
+  const bool norm = p.cfg.normalize, clamp = p.cfg.has_clamp;
+  const int grid = (int)L.total_tiles;
+#define GF_FWD(N, C, O) render_fwd_kernel<NF, N, C, O><<<grid, kRenderThreads, 0, st>>>(p)
+  if (cfg->out_dtype == GF_F32) {
+    if (norm) { if (clamp) GF_FWD(true, true, GF_F32); else GF_FWD(true, false, GF_F32); }
+    else { if (clamp) GF_FWD(false, true, GF_F32); else GF_FWD(false, false, GF_F32); }
+  } else {
+    if (norm) { if (clamp) GF_FWD(true, true, GF_BF16); else GF_FWD(true, false, GF_BF16); }
+    else { if (clamp) GF_FWD(false, true, GF_BF16); else GF_FWD(false, false, GF_BF16); }
+  }
+#undef GF_FWD
+  GF_LAUNCH_CHECK("render_fwd_kernel");
+  trace_mark(st);
+  return GF_OK;
+}
+
+template <int NF, bool N, bool C, int G>
+void launch_bwd_render(const Params<NF>& p, int grid, size_t smem, cudaStream_t st) {
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(render_bwd_kernel<NF, N, C, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         kBwdSmemCapFloats * 4);
+    attr_set = true;
+  }
+  render_bwd_kernel<NF, N, C, G><<<grid, kRenderThreads, smem, st>>>(p);
+}
+
+template <int NF>
+gf_status run_backward(const gf_config* cfg, const gf_batch* batch, const Layout& L, char* ws, cudaStream_t st) {
+  thread_local Params<NF>* tp = nullptr;
+  if (!tp) tp = new Params<NF>();
+  Params<NF>& p = *tp;
+  fill_params(p, cfg, batch, L, ws);
+  trace_mark(st);
+  bwd_prep_kernel<NF><<<p.n, kBinThreads, 0, st>>>(p);
+  GF_LAUNCH_CHECK("bwd_prep_kernel");
+  trace_mark(st);
+  const bool norm = p.cfg.normalize, clamp = p.cfg.has_clamp;
+  const int grid = (int)L.total_tiles;
+  const size_t smem = sizeof(float) * ((size_t)cfg->tile_out * cfg->tile_in + cfg->tile_out);
+#define GF_BWD(N, C, G) launch_bwd_render<NF, N, C, G>(p, grid, smem, st)
+  if (cfg->grad_dtype == GF_F32) {
+    if (norm) { if (clamp) GF_BWD(true, true, GF_F32); else GF_BWD(true, false, GF_F32); }
+    else { if (clamp) GF_BWD(false, true, GF_F32); else GF_BWD(false, false, GF_F32); }
+  } else {
+    if (norm) { if (clamp) GF_BWD(true, true, GF_BF16); else GF_BWD(true, false, GF_BF16); }
+    else { if (clamp) GF_BWD(false, true, GF_BF16); else GF_BWD(false, false, GF_BF16); }
+  }
+#undef GF_BWD
+  GF_LAUNCH_CHECK("render_bwd_kernel");
+  trace_mark(st);
+  if (L.total_g > 0) {
+    const int wpb = kRenderThreads / 32;
+    const int fgrid = (int)ceil_div(L.total_g, wpb);
+    if (norm) bwd_finalize_kernel<NF, true><<<fgrid, kRenderThreads, 0, st>>>(p);
+    else bwd_finalize_kernel<NF, false><<<fgrid, kRenderThreads, 0, st>>>(p);
+    GF_LAUNCH_CHECK("bwd_finalize_kernel");
+  }
+  trace_mark(st);
+  return GF_OK;
+}
+
+}  // namespace gf
+
+// ---------------------------------------------------------------------------
+// C ABI
+
+extern "C" {
+
+int gf_abi_version(void) { return GF_ABI_VERSION; }
+
+const char* gf_last_error(void) { return gf::g_last_error.c_str(); }
+
+int64_t gf_num_tiles(int64_t out_features, int64_t in_features, int64_t tile_out, int64_t tile_in) {
+  if (out_features <= 0 || in_features <= 0 || tile_out <= 0 || tile_in <= 0) return 0;
+  return gf::ceil_div(out_features, tile_out) * gf::ceil_div(in_features, tile_in);
+}
+
+size_t gf_workspace_bytes(const gf_config* cfg, const gf_batch* batch, gf_pass pass) {
+  if (gf::validate(cfg, batch, pass, /*data=*/false) != GF_OK) return 0;
+  return gf::layout(cfg, batch, pass).total;
+}
+
+static gf_status gf_dispatch(const gf_config* cfg, const gf_batch* batch, void* workspace, size_t workspace_bytes,
+                             gf_stream stream, gf_pass pass) {
+  gf_status s = gf::validate(cfg, batch, pass);
+  if (s != GF_OK) return s;
+  const gf::Layout L = gf::layout(cfg, batch, pass);
+  if (!workspace) return gf::fail(GF_ERR_INVALID_ARG, "workspace must be non-null");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return gf::fail(GF_ERR_INVALID_ARG, "workspace must be 256-byte aligned");
+  if (workspace_bytes < L.total)
+    return gf::fail(GF_ERR_INVALID_ARG, "workspace too small: %zu bytes given, %zu needed", workspace_bytes, L.total);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  const int n = batch->num_fields;
+  if (pass == GF_PASS_FORWARD) {
+    if (n == 1) return gf::run_forward<1>(cfg, batch, L, ws, st);
+    if (n <= 16) return gf::run_forward<16>(cfg, batch, L, ws, st);
+    return gf::run_forward<GF_MAX_FIELDS>(cfg, batch, L, ws, st);
+  }
+  if (n == 1) return gf::run_backward<1>(cfg, batch, L, ws, st);
+  if (n <= 16) return gf::run_backward<16>(cfg, batch, L, ws, st);
+  return gf::run_backward<GF_MAX_FIELDS>(cfg, batch, L, ws, st);
+}
+
+gf_status gf_forward(const gf_config* cfg, const gf_batch* batch, void* workspace, size_t workspace_bytes,
+                     gf_stream stream) {
+  return gf_dispatch(cfg, batch, workspace, workspace_bytes, stream, GF_PASS_FORWARD);
+}
+
+gf_status gf_backward(const gf_config* cfg, const gf_batch* batch, void* workspace, size_t workspace_bytes,
+                      gf_stream stream) {
+  return gf_dispatch(cfg, batch, workspace, workspace_bytes, stream, GF_PASS_BACKWARD);
+}
+
+gf_status gf_workspace_status(void* workspace, gf_stream stream, int reset, uint32_t* flags_out) {
+  if (!workspace || !flags_out) return gf::fail(GF_ERR_INVALID_ARG, "workspace and flags_out must be non-null");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  uint32_t flags = 0;
+  cudaError_t e = cudaMemcpyAsync(&flags, workspace, sizeof(flags), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && reset) {
+    e = cudaMemsetAsync(workspace, 0, sizeof(uint32_t), st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  }
+  if (e != cudaSuccess) return gf::fail(GF_ERR_CUDA, "gf_workspace_status: %s", cudaGetErrorString(e));
+  *flags_out = flags;
+  return GF_OK;
+}
+
+gf_status gf_trace_events(void* const* events, int n) {
+  if (n < 0 || (n > 0 && !events)) return gf::fail(GF_ERR_INVALID_ARG, "gf_trace_events: bad event array");
+  gf::g_trace.ev = events;
+  gf::g_trace.n = n;
+  gf::g_trace.used = 0;
+  return GF_OK;
+}
+
+int gf_trace_count(void) { return gf::g_trace.used; }
+
+}  // extern "C"

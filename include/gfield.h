@@ -1,0 +1,162 @@
+/*
+ * gfield.h -- C ABI of libgfield.so, the B200 (sm_100a) Gaussian-field
+ * weight-delta renderer.
+ *
+ * A field is one patched linear layer: K anisotropic 2-D Gaussians
+ * (mu [K,2], chol_raw [K,3], amp [K,1], all fp32) over the axes
+ * row_coords [out] and col_coords [in].  The forward renders
+ * delta [out*in] (row-major [out,in]) and the stable tile binning
+ * (tile_ptr [T+1], gaussian_ids_sorted [P]); the backward turns
+ * dL/d(delta) into d_mu [K,2], d_chol_raw [K,3], d_amp [K,1].
+ *
+ * Drop-in boundary: these entry points replace the pybind module
+ * `gaussian_peft_cuda_field_reference` of GUASS
+ * (gaussian_peft/cuda_field/csrc/ext.cpp:9-110, loaded by
+ * gaussian_peft/cuda_field/loader.py:96-109).  A Python shim
+ * (guass_b200/cuda_field) presents the same three methods on top of them.
+ *
+ * Conventions
+ *  - Every pointer inside gf_field / gf_batch is a DEVICE pointer unless
+ *    stated otherwise; the gf_field array itself lives in host memory and is
+ *    read during the call only.
+ *  - The caller owns all memory, including the scratch workspace, whose size
+ *    gf_workspace_bytes() returns.  The library never allocates or frees.
+ *  - All work is enqueued on `stream`; no call synchronises the stream except
+ *    gf_workspace_status().  Calls on different streams must use different
+ *    workspaces.
+ *  - A workspace must be zero-filled once after allocation; the kernels keep
+ *    their own counters consistent afterwards.
+ *  - Errors: every call returns a gf_status; gf_last_error() gives the
+ *    message of the last failure on the calling thread.  Conditions found on
+ *    the device (pair capacity, inconsistent saved binning) are recorded in
+ *    the workspace and read with gf_workspace_status().
+ */
+#ifndef GFIELD_H
+#define GFIELD_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GF_ABI_VERSION 1
+/* Upper bound on fields per call (one kernel-parameter descriptor each). */
+#define GF_MAX_FIELDS 192
+
+typedef struct CUstream_st* gf_stream; /* == cudaStream_t */
+
+typedef enum gf_status {
+  GF_OK = 0,
+  GF_ERR_INVALID_ARG = 1, /* bad pointer, shape or config (TORCH_CHECK in the reference) */
+  GF_ERR_CAPACITY = 2,    /* gaussian_ids buffer smaller than the pair count */
+  GF_ERR_CUDA = 3,        /* a CUDA runtime call or launch failed */
+  GF_ERR_STATE = 4,       /* saved binning inconsistent with the parameters */
+  GF_ERR_UNSUPPORTED = 5  /* request outside the implemented envelope */
+} gf_status;
+
+typedef enum gf_dtype { GF_F32 = 0, GF_BF16 = 1 } gf_dtype;
+
+/* Device-side condition bits returned by gf_workspace_status(). */
+#define GF_FLAG_CAPACITY 0x1u /* pairs exceeded ids capacity; ids truncated */
+#define GF_FLAG_STATE 0x2u    /* backward: tile_ptr/ids do not match mu/chol_raw */
+#define GF_FLAG_INTERNAL 0x4u /* forward: per-tile list disagreed with tile_ptr */
+
+/* Render options; mirrors ForwardConfig (gaussian_peft/cuda_field/csrc/field.h:11-18)
+ * plus the output/gradient storage types. */
+typedef struct gf_config {
+  int64_t tile_out;        /* > 0 */
+  int64_t tile_in;         /* > 0 */
+  double sigma_multiplier; /* > 0 */
+  int32_t normalize;       /* multiply the basis by 1/(2*pi*sqrt(det)) */
+  int32_t has_clamp_quad;  /* clamp the quadratic form at clamp_quad */
+  double clamp_quad;
+  float out_scale;    /* delta is stored as out_scale * value (1.0 = reference) */
+  int32_t out_dtype;  /* gf_dtype of delta */
+  int32_t grad_dtype; /* gf_dtype of grad_delta */
+} gf_config;
+
+/* One field (layer).  Forward reads the inputs and writes delta, tile_ptr and
+ * (in per-field id mode) gaussian_ids; backward reads grad_delta, tile_ptr and
+ * the ids and writes d_mu, d_chol_raw, d_amp. */
+typedef struct gf_field {
+  int64_t out_features; /* rows of delta, > 0 */
+  int64_t in_features;  /* cols of delta, > 0 */
+  int64_t num_gaussians;/* K >= 0 */
+  const float* row_coords; /* [out] */
+  const float* col_coords; /* [in] */
+  const float* mu;         /* [K,2] */
+  const float* chol_raw;   /* [K,3] */
+  const float* amp;        /* [K] */
+  void* delta;             /* [out*in] out_dtype (forward output) */
+  int64_t* tile_ptr;       /* [T+1], T = ceil(out/tile_out)*ceil(in/tile_in) */
+  int64_t* gaussian_ids;   /* per-field id mode: [ids_capacity] */
+  int64_t ids_capacity;    /* forward: capacity; backward: number of pairs */
+  const void* grad_delta;  /* [out*in] grad_dtype (backward input) */
+  float* d_mu;             /* [K,2] (backward output) */
+  float* d_chol_raw;       /* [K,3] (backward output) */
+  float* d_amp;            /* [K]   (backward output) */
+} gf_field;
+
+/* A batch of fields rendered by one set of launches.
+ * Id mode: when `ids` is NULL, each field uses its own gaussian_ids /
+ * ids_capacity.  When `ids` is non-NULL, all fields share it: the forward
+ * writes field f's pairs at ids[pair_base[f] ...] and pair_base [n+1]
+ * (device, exclusive prefix of the per-field pair counts), and the backward
+ * reads both back. */
+typedef struct gf_batch {
+  int32_t num_fields;      /* 1 .. GF_MAX_FIELDS */
+  const gf_field* fields;  /* HOST array of num_fields descriptors */
+  int64_t* ids;            /* shared id buffer or NULL */
+  int64_t ids_capacity;    /* its length */
+  int64_t* pair_base;      /* [num_fields+1] device, used with `ids` */
+} gf_batch;
+
+typedef enum gf_pass { GF_PASS_FORWARD = 0, GF_PASS_BACKWARD = 1 } gf_pass;
+
+/* ABI version compiled into the library (GF_ABI_VERSION). */
+int gf_abi_version(void);
+
+/* Message for the last non-OK status returned on this thread. */
+const char* gf_last_error(void);
+
+/* Number of tiles of a field: ceil(out/tile_out) * ceil(in/tile_in). */
+int64_t gf_num_tiles(int64_t out_features, int64_t in_features, int64_t tile_out, int64_t tile_in);
+
+/* Bytes of scratch workspace a pass needs for this batch. */
+size_t gf_workspace_bytes(const gf_config* cfg, const gf_batch* batch, gf_pass pass);
+
+/* Forward render.  Replaces gaussian_field_forward
+ * (gaussian_peft/cuda_field/csrc/ext.cpp:9-37, field_impl.cu:135-163,
+ * forward.cu:372-569): per-Gaussian preprocess, stable tile binning and the
+ * tile render, for every field of the batch.  delta is fully written (no
+ * pre-zeroing needed).  tile_ptr values are relative to the field's own ids. */
+gf_status gf_forward(const gf_config* cfg, const gf_batch* batch, void* workspace,
+                     size_t workspace_bytes, gf_stream stream);
+
+/* Training backward.  Replaces gaussian_field_backward
+ * (gaussian_peft/cuda_field/csrc/ext.cpp:38-72, field_impl.cu:165-179,
+ * backward.cu:541-716).  Reads the binning saved by gf_forward; the
+ * gradients are reduced in a fixed order (bitwise reproducible). */
+gf_status gf_backward(const gf_config* cfg, const gf_batch* batch, void* workspace,
+                      size_t workspace_bytes, gf_stream stream);
+
+/* Synchronises `stream`, returns the device condition bits (GF_FLAG_*)
+ * accumulated in `workspace` since the last reset, optionally clearing them. */
+gf_status gf_workspace_status(void* workspace, gf_stream stream, int reset, uint32_t* flags_out);
+
+/* Profiling hook (no reference counterpart; the reference has no timing
+ * facility).  After this call, gf_forward / gf_backward on the calling thread
+ * record the caller's CUDA events (cudaEvent_t, passed as void*) on their
+ * stream: one before their first kernel and one after each kernel
+ * (forward: 3 = start, bin, render; backward: 4 = start, prep, render,
+ * finalize), consuming events[0..n) in order until all n are used.  n = 0
+ * turns tracing off.  gf_trace_count() returns how many have been recorded. */
+gf_status gf_trace_events(void* const* events, int n);
+int gf_trace_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

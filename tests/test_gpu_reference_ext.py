@@ -1,0 +1,100 @@
+"""CUDA product path vs GUASS's own CUDA extension, on the same B200.
+
+oracle/build_ref.py compiles the reference's unmodified
+gaussian_peft/cuda_field/csrc sources into oracle/_ref/ (in the build
+container, where the sources are mounted).  These tests load that module and
+compare on identical inputs:
+  * tile_ptr and gaussian_ids_sorted: bit-exact;
+  * fp32 delta: bit-exact (same per-element operation sequence and expf);
+  * gradients: within 1e-5 of channel scale (different reduction order).
+They are skipped when the reference build is not present.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from guass_b200 import synthetic as S
+from gpu_helpers import (assert_grads_exact_within, exact_grads, random_field, reference_undefined_tiles, run_ext,
+                         tile_mask_to_elements)
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ref_ext():
+    try:
+        from oracle import build_ref
+        return build_ref.load()
+    except (FileNotFoundError, ImportError, OSError) as e:
+        pytest.skip(f"reference extension not available: {e}")
+
+
+def run_ref(ext, f, tile_out=32, tile_in=32, sigma=3.0, normalize=False, clamp=80.0):
+    d = f.to("cuda")
+    delta, tp, ids = ext.gaussian_field_forward(d.row_coords, d.col_coords, d.mu, d.chol_raw, d.amp, tile_out,
+                                                tile_in, sigma, normalize, clamp)
+    grads = ext.gaussian_field_backward(d.grad, d.row_coords, d.col_coords, d.mu, d.chol_raw, d.amp, tp, ids,
+                                        tile_out, tile_in, sigma, normalize, clamp)
+    torch.cuda.synchronize()
+    return delta.cpu().numpy(), tp.cpu().numpy(), ids.cpu().numpy(), [g.cpu().numpy() for g in grads]
+
+
+def _compare(ref_ext, f, label, **kw):
+    a = run_ext(f, **kw)
+    b = run_ref(ref_ext, f, **kw)
+    np.testing.assert_array_equal(a[1], b[1])
+    np.testing.assert_array_equal(a[2], b[2])
+    to, ti = kw.get("tile_out", 32), kw.get("tile_in", 32)
+    undefined = tile_mask_to_elements(reference_undefined_tiles(f.out_features, f.in_features, to, ti, a[1]),
+                                      f.out_features, f.in_features, to, ti)
+    differ = a[0].view(np.uint32) != b[0].view(np.uint32)
+    # bit-exact wherever the reference's result is defined
+    assert not (differ & ~undefined).any(), \
+        f"{int((differ & ~undefined).sum())} delta elements differ bitwise outside reference-undefined tiles"
+    exact = exact_grads(f, a[1], a[2], **{k: v for k, v in kw.items() if k in ("tile_out", "tile_in", "sigma",
+                                                                              "normalize", "clamp")})
+    assert_grads_exact_within(a[3], exact, label=f"gpu_vs_exact:{label}:")
+    assert_grads_exact_within(b[3], exact, label=f"ref_vs_exact:{label}:")
+
+
+@pytest.mark.parametrize("cfg", ["cfg0", "cfg1", "cfg2"])
+def test_configs_match_reference_extension(ref_ext, cfg):
+    _compare(ref_ext, S.CONFIGS[cfg](), cfg)
+
+
+@pytest.mark.parametrize("normalize,clamp", [(True, 80.0), (False, None), (True, None)])
+def test_variants_match_reference_extension(ref_ext, normalize, clamp):
+    _compare(ref_ext, random_field(200, 300, 80, seed=11, mean_scale=0.08), f"variant_{normalize}_{clamp}",
+             normalize=normalize, clamp=clamp)
+
+
+@pytest.mark.parametrize("shape,tiles", [((70, 45), (16, 8)), ((33, 130), (32, 32)), ((100, 200), (64, 64)),
+                                         ((90, 77), (7, 13))])
+def test_tile_shapes_match_reference_extension(ref_ext, shape, tiles):
+    _compare(ref_ext, random_field(shape[0], shape[1], 30, seed=5, mean_scale=0.1), f"tiles_{shape}_{tiles}",
+             tile_out=tiles[0], tile_in=tiles[1])
+
+
+def test_binning_bit_exact_at_scale(ref_ext):
+    """60k random Gaussians of widely varying size and shape on a 2048x3072
+    field: every floor/ceil of the 3-sigma box must land where the reference's
+    does."""
+    g = torch.Generator().manual_seed(123)
+    k = 60_000
+    out_f, in_f = 2048, 3072
+    mu = (torch.rand(k, 2, generator=g) * 2.4 - 1.2).cuda()
+    chol = torch.stack([torch.randn(k, generator=g) * 1.5 - 4.0, torch.randn(k, generator=g) * 0.05,
+                        torch.randn(k, generator=g) * 1.5 - 4.0], 1).cuda().contiguous()
+    amp = (torch.randn(k, 1, generator=g) * 1e-3).cuda()
+    row = torch.linspace(-1, 1, out_f).cuda()
+    col = torch.linspace(-1, 1, in_f).cuda()
+    from guass_b200.cuda_field import load_extension
+    mine = load_extension().gaussian_field_forward(row, col, mu, chol, amp, 32, 32, 3.0, False, 80.0)
+    theirs = ref_ext.gaussian_field_forward(row, col, mu, chol, amp, 32, 32, 3.0, False, 80.0)
+    assert torch.equal(mine[1], theirs[1])
+    assert torch.equal(mine[2], theirs[2])
+    assert torch.equal(mine[0].view(torch.int32), theirs[0].view(torch.int32))
