@@ -14,6 +14,7 @@ LIB_PATH = PKG / "libgfield.so"
 
 GF_ABI_VERSION = 1
 GF_MAX_FIELDS = 192
+GF_NOALLOC_SCRATCH_BYTES = 4 << 20
 
 GF_OK = 0
 GF_ERR_INVALID_ARG = 1
@@ -35,7 +36,8 @@ GF_FLAG_INTERNAL = 0x4
 
 # Every symbol include/gfield.h declares.
 EXPORTED = ("gf_abi_version", "gf_last_error", "gf_num_tiles", "gf_workspace_bytes", "gf_forward",
-            "gf_backward", "gf_workspace_status", "gf_trace_events", "gf_trace_count")
+            "gf_backward", "gf_workspace_status", "gf_trace_events", "gf_trace_count",
+            "gf_forward_noalloc")
 
 
 class GfConfig(ctypes.Structure):
@@ -120,6 +122,8 @@ def lib() -> ctypes.CDLL:
     L.gf_trace_events.restype = ctypes.c_int
     L.gf_trace_count.argtypes = []
     L.gf_trace_count.restype = ctypes.c_int
+    L.gf_forward_noalloc.argtypes = [ctypes.POINTER(GfConfig), ctypes.POINTER(GfBatch), ctypes.c_void_p]
+    L.gf_forward_noalloc.restype = ctypes.c_int
     if L.gf_abi_version() != GF_ABI_VERSION:
         raise ImportError(f"libgfield ABI {L.gf_abi_version()} != expected {GF_ABI_VERSION}")
     _lib = L

@@ -23,6 +23,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 namespace gf {
@@ -1030,3 +1031,93 @@ gf_status gf_trace_events(void* const* events, int n) {
 int gf_trace_count(void) { return gf::g_trace.used; }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Forward render without caller scratch (gf_forward_noalloc).
+//
+// For callers that are handed their input and output buffers by a host that
+// owns all device memory (an inference-engine plugin, a framework custom call,
+// a runtime with a fixed memory budget) and that may not call cudaMalloc or
+// ask for a workspace.  The forward's scratch then lives in this file-scope
+// array, which every GPU that loads the library holds until the process
+// exits.  All calls share it: two calls whose work overlaps on the GPU (other
+// streams, other host threads) race on it and must be ordered by the caller.
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[GF_NOALLOC_SCRATCH_BYTES];
+
+namespace gf {
+
+constexpr int kNoallocMaxDevices = 64;
+void* g_noalloc_ptr[kNoallocMaxDevices];  // device address of the array, per device
+std::mutex g_noalloc_mutex;               // guards the pointers and the static descriptors
+Params<1> g_noalloc_p1;                    // launch descriptors in static storage:
+Params<16> g_noalloc_p16;                  // no heap allocation on this path
+Params<GF_MAX_FIELDS> g_noalloc_pmax;
+
+template <int NF>
+gf_status noalloc_launch(Params<NF>& p, const gf_config* cfg, const gf_batch* batch, const Layout& L, char* ws,
+                         cudaStream_t st) {
+  fill_params(p, cfg, batch, L, ws);
+  int max_nd = 0;
+  for (int i = 0; i < p.n; ++i) {
+    const int nd = (p.f[i].ntr + 1) * (p.f[i].ntc + 1);
+    if (nd <= kBinSmemCapInts && nd > max_nd) max_nd = nd;
+  }
+  cudaError_t e = cudaFuncSetAttribute(bin_kernel<NF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kBinSmemCapInts * 4);
+  if (e != cudaSuccess) return fail(GF_ERR_CUDA, "gf_forward_noalloc: %s", cudaGetErrorString(e));
+  bin_kernel<NF><<<p.n, kBinThreads, sizeof(int) * (size_t)max_nd, st>>>(p, kBinSmemCapInts);
+  GF_LAUNCH_CHECK("bin_kernel");
+  const bool norm = p.cfg.normalize, clamp = p.cfg.has_clamp;
+  const int grid = (int)L.total_tiles;
+#define GF_FWD(N, C, O) render_fwd_kernel<NF, N, C, O><<<grid, kRenderThreads, 0, st>>>(p)
+  if (cfg->out_dtype == GF_F32) {
+    if (norm) { if (clamp) GF_FWD(true, true, GF_F32); else GF_FWD(true, false, GF_F32); }
+    else { if (clamp) GF_FWD(false, true, GF_F32); else GF_FWD(false, false, GF_F32); }
+  } else {
+    if (norm) { if (clamp) GF_FWD(true, true, GF_BF16); else GF_FWD(true, false, GF_BF16); }
+    else { if (clamp) GF_FWD(false, true, GF_BF16); else GF_FWD(false, false, GF_BF16); }
+  }
+#undef GF_FWD
+  GF_LAUNCH_CHECK("render_fwd_kernel");
+  return GF_OK;
+}
+
+}  // namespace gf
+
+extern "C" gf_status gf_forward_noalloc(const gf_config* cfg, const gf_batch* batch, gf_stream stream) {
+  gf_status s = gf::validate(cfg, batch, GF_PASS_FORWARD);
+  if (s != GF_OK) return s;
+  const gf::Layout L = gf::layout(cfg, batch, GF_PASS_FORWARD);
+  if (L.total > (size_t)GF_NOALLOC_SCRATCH_BYTES)
+    return gf::fail(GF_ERR_UNSUPPORTED,
+                    "gf_forward_noalloc: this batch needs %zu bytes of scratch but the static scratch holds %zu; "
+                    "use gf_forward with a caller workspace",
+                    L.total, (size_t)GF_NOALLOC_SCRATCH_BYTES);
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return gf::fail(GF_ERR_CUDA, "gf_forward_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= gf::kNoallocMaxDevices)
+    return gf::fail(GF_ERR_UNSUPPORTED, "gf_forward_noalloc: device %d beyond the supported %d", dev,
+                    gf::kNoallocMaxDevices);
+  std::lock_guard<std::mutex> lock(gf::g_noalloc_mutex);
+  if (gf::g_noalloc_ptr[dev] == nullptr) {
+    // One-time set-up on this device (the device is current): the array's
+    // name is only a host-side stand-in, so fetch its device address.
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || ptr == nullptr)
+      return gf::fail(GF_ERR_CUDA, "gf_forward_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    gf::g_noalloc_ptr[dev] = ptr;
+  }
+  char* ws = static_cast<char*>(gf::g_noalloc_ptr[dev]);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // The array keeps the previous call's contents; the status word and the
+  // completion counter in its header must start at zero.
+  e = cudaMemsetAsync(ws + L.hdr, 0, 256, st);
+  if (e != cudaSuccess) return gf::fail(GF_ERR_CUDA, "gf_forward_noalloc: cudaMemsetAsync: %s", cudaGetErrorString(e));
+  const int n = batch->num_fields;
+  if (n == 1) return gf::noalloc_launch(gf::g_noalloc_p1, cfg, batch, L, ws, st);
+  if (n <= 16) return gf::noalloc_launch(gf::g_noalloc_p16, cfg, batch, L, ws, st);
+  return gf::noalloc_launch(gf::g_noalloc_pmax, cfg, batch, L, ws, st);
+}

@@ -156,6 +156,26 @@ gf_status gf_workspace_status(void* workspace, gf_stream stream, int reset, uint
 gf_status gf_trace_events(void* const* events, int n);
 int gf_trace_count(void);
 
+/* Bytes of the library's static forward scratch (see gf_forward_noalloc). */
+#define GF_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/* Forward render that allocates nothing.  No counterpart in the reference:
+ * it exists for callers that cannot allocate device memory or supply a
+ * workspace -- code running inside a host that owns all device memory and
+ * only hands it input and output buffers (inference-engine plugins,
+ * framework custom calls, fixed-budget runtimes).  Same inputs, outputs and
+ * results as gf_forward; the scratch gf_forward takes as `workspace` is a
+ * 4 MiB array inside the library instead, held by every GPU that loads the
+ * library until the process exits.  Batches whose forward scratch
+ * (gf_workspace_bytes(cfg, batch, GF_PASS_FORWARD)) exceeds
+ * GF_NOALLOC_SCRATCH_BYTES are rejected with GF_ERR_UNSUPPORTED; in per-field
+ * id mode a caller detects an id buffer that was too small by reading
+ * tile_ptr[T] (the pair count) after the call.  The first call on a device
+ * looks up the array's device address on that device, so make it before any
+ * stream capture.  All calls share the one array: calls whose work overlaps
+ * on the GPU race on it and must be ordered by the caller. */
+gf_status gf_forward_noalloc(const gf_config* cfg, const gf_batch* batch, gf_stream stream);
+
 #ifdef __cplusplus
 }
 #endif
