@@ -457,6 +457,189 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
 }
 
 // ---------------------------------------------------------------------------
+// Packed fp32x2 arithmetic (sm_100: one issue slot for two IEEE fp32
+// operations, each rounded exactly like the scalar instruction).
+
+typedef unsigned long long f2;
+
+__device__ __forceinline__ f2 pk2(float a, float b) {
+  f2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void up2(f2 x, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(x));
+}
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
+  f2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ f2 mul2(f2 a, f2 b) {
+  f2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2 add2(f2 a, f2 b) {
+  f2 d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2 sub2(f2 a, f2 b) {
+  f2 d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// ---------------------------------------------------------------------------
+// Forward kernel 2, 32x32-tile fast path: one CTA of kFwd32Warps warps per
+// tile, warp w owning rows [w*R, (w+1)*R) and lane = column.  Each warp walks
+// the candidate Gaussians 32 at a time, tests their boxes, and consumes the
+// warp ballot's set bits in ascending order -- the reference's stable-sorted
+// order -- so no shared list and no CTA barrier are needed.  Per Gaussian the
+// column terms (dy and the two products with it) are computed once per lane;
+// per pair of rows the quadratic form is evaluated with packed fp32x2
+// instructions in exactly the reference's association, expf and the
+// accumulation stay scalar and sequential: the fp32 output is bit-identical
+// to the generic kernel's and to the reference's.
+constexpr int kFwd32Warps = 2;
+
+template <int NF, bool NORM, bool CLAMP, int OUTT>
+__global__ void __launch_bounds__(32 * kFwd32Warps)
+render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
+  constexpr int R = 32 / kFwd32Warps;  // rows per warp
+  __shared__ __align__(16) float s_out[kFwd32Warps][R][36];
+  const int tg = blockIdx.x;
+  const int fi = field_of_tile(p, tg);
+  const DevField& F = p.f[fi];
+  const int t = tg - F.tile_base;
+  const int tr = t / F.ntc, tc = t % F.ntc;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int row0 = tr * 32, col0 = tc * 32;
+  const int th = min(32, F.out_f - row0), tw = min(32, F.in_f - col0);
+  const int64_t start = F.tile_ptr[t];
+  const int64_t count = F.tile_ptr[t + 1] - start;
+  int64_t* ids;
+  int64_t cap_left;
+  if (p.batch_ids != nullptr) {
+    const int64_t b = p.pair_base[fi];
+    ids = p.batch_ids + b + start;
+    cap_left = p.batch_cap - b - start;
+  } else {
+    ids = F.ids + start;
+    cap_left = F.ids_cap - start;
+  }
+  const float4* rec = p.records + 2 * (size_t)F.g_base;
+  const int4* box = p.boxes + F.g_base;
+  const float nclamp = p.cfg.nclamp;
+  const int rw0 = warp * R;
+  const float cc = (lane < tw) ? F.col[col0 + lane] : 0.0f;
+  const float myr = (lane < R && rw0 + lane < th) ? F.row[row0 + rw0 + lane] : 0.0f;
+  f2 CR[R / 2];
+#pragma unroll
+  for (int i = 0; i < R / 2; ++i)
+    CR[i] = pk2(__shfl_sync(0xffffffffu, myr, 2 * i), __shfl_sync(0xffffffffu, myr, 2 * i + 1));
+  float v[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) v[i] = 0.0f;
+
+  int64_t found = 0;
+  for (int k0 = 0; k0 < F.K && found < count; k0 += 32) {
+    const int g = k0 + lane;
+    bool hit = false;
+    if (g < F.K) {
+      const int4 b = box[g];
+      hit = (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
+    }
+    unsigned m = __ballot_sync(0xffffffffu, hit);
+    if (warp == 0 && hit) {
+      const int64_t pos = found + __popc(m & ((1u << lane) - 1u));
+      if (pos < cap_left) ids[pos] = g;
+    }
+    found += __popc(m);
+    while (m) {
+      const int gg = k0 + __ffs(m) - 1;
+      m &= m - 1;
+      const float4 a = rec[2 * gg];
+      const float4 h = rec[2 * gg + 1];
+      const float dy = __fsub_rn(cc, a.y);
+      const float a01 = __fmul_rn(h.y, dy);
+      const float a11 = __fmul_rn(h.z, dy);
+      const f2 H00 = pk2(h.x, h.x), H01 = pk2(h.y, h.y), A01 = pk2(a01, a01), A11 = pk2(a11, a11);
+      const f2 DY = pk2(dy, dy), MUR = pk2(a.x, a.x);
+#pragma unroll
+      for (int i = 0; i < R / 2; ++i) {
+        const f2 DX = sub2(CR[i], MUR);
+        const f2 T1 = fma2(H00, DX, A01);
+        const f2 T2 = fma2(H01, DX, A11);
+        const f2 Q = fma2(DX, T1, mul2(DY, T2));
+        float q0, q1;
+        up2(Q, q0, q1);
+        q0 = fminf(q0, 0.0f);
+        q1 = fminf(q1, 0.0f);
+        if (CLAMP) {
+          q0 = fmaxf(q0, nclamp);
+          q1 = fmaxf(q1, nclamp);
+        }
+        float e0 = expf(q0), e1 = expf(q1);
+        if (NORM) {
+          e0 = __fmul_rn(e0, a.w);
+          e1 = __fmul_rn(e1, a.w);
+        }
+        v[2 * i] = __fmaf_rn(a.z, e0, v[2 * i]);
+        v[2 * i + 1] = __fmaf_rn(a.z, e1, v[2 * i + 1]);
+      }
+    }
+  }
+  if (warp == 0 && lane == 0 && found != count) atomicOr(p.status, GF_FLAG_INTERNAL);
+
+  // Stage the warp's R x 32 block and store it with 128-bit stores.
+  const float sc = p.cfg.out_scale;
+#pragma unroll
+  for (int i = 0; i < R; ++i) s_out[warp][i][lane] = (sc != 1.0f) ? __fmul_rn(v[i], sc) : v[i];
+  __syncwarp();
+  const int bh = min(R, th - rw0);
+  if (bh <= 0) return;
+  const size_t base = (size_t)(row0 + rw0) * F.in_f + col0;
+  if (OUTT == GF_F32) {
+    float* out = reinterpret_cast<float*>(F.delta) + base;
+#pragma unroll
+    for (int k = 0; k < R / 4; ++k) {
+      const int r = k * 4 + (lane >> 3), q4 = (lane & 7) * 4;
+      if (r < bh) {
+        if (F.vec_ok && q4 + 3 < tw) {
+          *reinterpret_cast<float4*>(out + (size_t)r * F.in_f + q4) =
+              *reinterpret_cast<const float4*>(&s_out[warp][r][q4]);
+        } else {
+          for (int j = 0; j < 4; ++j)
+            if (q4 + j < tw) out[(size_t)r * F.in_f + q4 + j] = s_out[warp][r][q4 + j];
+        }
+      }
+    }
+  } else {
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(F.delta) + base;
+#pragma unroll
+    for (int k = 0; k < R / 8; ++k) {
+      const int r = k * 8 + (lane >> 2), q8 = (lane & 3) * 8;
+      if (r < bh) {
+        if (F.vec_ok && q8 + 7 < tw) {
+          const float4 x0 = *reinterpret_cast<const float4*>(&s_out[warp][r][q8]);
+          const float4 x1 = *reinterpret_cast<const float4*>(&s_out[warp][r][q8 + 4]);
+          const __nv_bfloat162 h0 = __floats2bfloat162_rn(x0.x, x0.y), h1 = __floats2bfloat162_rn(x0.z, x0.w);
+          const __nv_bfloat162 h2 = __floats2bfloat162_rn(x1.x, x1.y), h3 = __floats2bfloat162_rn(x1.z, x1.w);
+          *reinterpret_cast<uint4*>(out + (size_t)r * F.in_f + q8) =
+              make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
+                         *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3));
+        } else {
+          for (int j = 0; j < 8; ++j)
+            if (q8 + j < tw) out[(size_t)r * F.in_f + q8 + j] = __float2bfloat16_rn(s_out[warp][r][q8 + j]);
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Backward kernel 1: per-field preprocess (backward.cu:552-557 rebuilds the
 // geometry too), plus each Gaussian's first slot in the pair-partial buffer:
 // an exclusive scan of tiles_touched, i.e. the reference's pair emission
@@ -631,6 +814,162 @@ render_bwd_kernel(const __grid_constant__ Params<NF> p) {
 }
 
 // ---------------------------------------------------------------------------
+// Backward kernel 2, 32x32-tile fast path: one CTA of kBwd32Warps warps per
+// tile; warp w handles the tile's pairs w, w+W, ...  Every lane keeps its
+// column of dL/d(delta) (32 rows) and the 32 row coordinates in registers
+// for the whole tile, so the per-element loop touches no memory.  Row pairs
+// use packed fp32x2 arithmetic; the basis is evaluated exactly as in the
+// forward.  The next pair's id is fetched while the current pair is
+// computed.  The six per-pair channels are reduced across the warp with a
+// reduce-scatter (9 shuffles instead of 30); lanes 0, 4, ..., 28 then hold
+// channels 0..7 and write the pair's slot with one 32-byte store.
+constexpr int kBwd32Warps = 4;
+
+template <int NF, bool NORM, bool CLAMP, int GT>
+__global__ void __launch_bounds__(32 * kBwd32Warps)
+render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
+  const int tg = blockIdx.x;
+  const int fi = field_of_tile(p, tg);
+  const DevField& F = p.f[fi];
+  const int t = tg - F.tile_base;
+  const int tr = t / F.ntc, tc = t % F.ntc;
+  const int64_t start = F.tile_ptr[t];
+  const int64_t count = F.tile_ptr[t + 1] - start;
+  if (count <= 0) return;
+  const int64_t id_base = (p.batch_ids != nullptr) ? p.pair_base[fi] : 0;
+  const int64_t id_limit = (p.batch_ids != nullptr) ? p.batch_cap : F.ids_cap;
+  if (start < 0 || id_base < 0 || id_base + start + count > id_limit) {
+    if (threadIdx.x == 0) atomicOr(p.status, GF_FLAG_STATE);
+    return;
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (warp >= count) return;
+  const int row0 = tr * 32, col0 = tc * 32;
+  const int th = min(32, F.out_f - row0), tw = min(32, F.in_f - col0);
+  const bool cval = lane < tw;
+  const float cc = cval ? F.col[col0 + lane] : 0.0f;
+  const float myr = (lane < th) ? F.row[row0 + lane] : 0.0f;
+  f2 CR[16], G2[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    CR[i] = pk2(__shfl_sync(0xffffffffu, myr, 2 * i), __shfl_sync(0xffffffffu, myr, 2 * i + 1));
+    const int r0 = 2 * i, r1 = 2 * i + 1;
+    const size_t e0 = (size_t)(row0 + r0) * F.in_f + col0 + lane;
+    const size_t e1 = (size_t)(row0 + r1) * F.in_f + col0 + lane;
+    const float g0 = (cval && r0 < th) ? load_grad<GT>(F.grad, e0) : 0.0f;
+    const float g1 = (cval && r1 < th) ? load_grad<GT>(F.grad, e1) : 0.0f;
+    G2[i] = pk2(g0, g1);
+  }
+  const int64_t* ids = ((p.batch_ids != nullptr) ? p.batch_ids : F.ids) + id_base + start;
+  const float4* rec = p.records + 2 * (size_t)F.g_base;
+  const int4* box = p.boxes + F.g_base;
+  const float nclamp = p.cfg.nclamp;
+  // channel held by this lane after the reduce-scatter: bits 4,3,2 of lane
+  const int my_ch = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+
+  int64_t gid = ids[warp];
+  for (int64_t i = warp; i < count; i += kBwd32Warps) {
+    const int64_t cur = gid;
+    const int64_t prev = (i > 0) ? ids[i - 1] : -1;
+    if (i + kBwd32Warps < count) gid = ids[i + kBwd32Warps];
+    bool ok = (cur >= 0) && (cur < F.K) && (prev < cur);
+    int4 b = make_int4(0, -1, 0, -1);
+    if (ok) {
+      b = box[cur];
+      ok = (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
+    }
+    if (!ok) {
+      if (lane == 0) atomicOr(p.status, GF_FLAG_STATE);
+      continue;
+    }
+    const float4 a = rec[2 * cur];
+    const float4 h = rec[2 * cur + 1];
+    const float dy = cval ? __fsub_rn(cc, a.y) : 0.0f;
+    const float a01 = __fmul_rn(h.y, dy);
+    const float a11 = __fmul_rn(h.z, dy);
+    const f2 H00 = pk2(h.x, h.x), H01 = pk2(h.y, h.y), A01 = pk2(a01, a01), A11 = pk2(a11, a11);
+    const f2 DY = pk2(dy, dy), MUR = pk2(a.x, a.x);
+    const f2 zero2 = pk2(0.0f, 0.0f);
+    f2 T0 = zero2, U0 = zero2, U1 = zero2, U2 = zero2;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const f2 DX = sub2(CR[k], MUR);
+      const f2 T1 = fma2(H00, DX, A01);
+      const f2 T2 = fma2(H01, DX, A11);
+      const f2 Q = fma2(DX, T1, mul2(DY, T2));
+      float q0, q1;
+      up2(Q, q0, q1);
+      q0 = fminf(q0, 0.0f);
+      q1 = fminf(q1, 0.0f);
+      bool act0 = true, act1 = true;
+      if (CLAMP) {
+        act0 = q0 > nclamp;  // reference: quad < clamp
+        act1 = q1 > nclamp;
+        q0 = fmaxf(q0, nclamp);
+        q1 = fmaxf(q1, nclamp);
+      }
+      float e0 = expf(q0), e1 = expf(q1);
+      if (NORM) {
+        e0 = __fmul_rn(e0, a.w);
+        e1 = __fmul_rn(e1, a.w);
+      }
+      const f2 GB = mul2(G2[k], pk2(e0, e1));
+      T0 = add2(T0, GB);
+      f2 GBA = GB;
+      if (CLAMP) {
+        float b0, b1;
+        up2(GB, b0, b1);
+        GBA = pk2(act0 ? b0 : 0.0f, act1 ? b1 : 0.0f);
+      }
+      U0 = add2(U0, GBA);
+      U1 = fma2(GBA, DX, U1);
+      U2 = fma2(mul2(GBA, DX), DX, U2);
+    }
+    float t0a, t0b, u0a, u0b, u1a, u1b, u2a, u2b;
+    up2(T0, t0a, t0b);
+    up2(U0, u0a, u0b);
+    up2(U1, u1a, u1b);
+    up2(U2, u2a, u2b);
+    const float t0 = t0a + t0b, u0 = u0a + u0b, u1 = u1a + u1b, u2 = u2a + u2b;
+    const float i00 = -2.0f * h.x, i01 = -2.0f * h.y, i11 = -2.0f * h.z;
+    const float dyU0 = dy * u0;
+    float ch[8] = {t0, i00 * u1 + i01 * dyU0, i01 * u1 + i11 * dyU0, u2, dy * u1, dy * dyU0, 0.0f, 0.0f};
+    // reduce-scatter over the warp: 8 -> 4 -> 2 -> 1 channels, then 4-lane sums
+    {
+      const bool hi = (lane >> 4) & 1;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float keep = hi ? ch[4 + k] : ch[k];
+        const float send = hi ? ch[k] : ch[4 + k];
+        ch[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+      }
+    }
+    {
+      const bool hi = (lane >> 3) & 1;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const float keep = hi ? ch[2 + k] : ch[k];
+        const float send = hi ? ch[k] : ch[2 + k];
+        ch[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      }
+    }
+    {
+      const bool hi = (lane >> 2) & 1;
+      const float keep = hi ? ch[1] : ch[0];
+      const float send = hi ? ch[0] : ch[1];
+      ch[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    ch[0] += __shfl_xor_sync(0xffffffffu, ch[0], 2);
+    ch[0] += __shfl_xor_sync(0xffffffffu, ch[0], 1);
+    const int64_t slot = p.goff[F.g_base + cur] + (int64_t)(tr - b.x) * (b.w - b.z + 1) + (tc - b.z);
+    if (slot >= 0 && slot < p.part_cap) {
+      if ((lane & 3) == 0) reinterpret_cast<float*>(p.partials)[8 * slot + my_ch] = ch[0];
+    } else if (lane == 0) {
+      atomicOr(p.status, GF_FLAG_STATE);
+    }
+  }
+}
+
 // Backward kernel 3: one warp per Gaussian.  Sums the Gaussian's pair
 // partials (contiguous, fixed order) in fp64, applies amp and -0.5, and
 // evaluates the covariance chain of backward.cu:436-496 in fp64 before the
@@ -891,7 +1230,12 @@ gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout&
   trace_mark(st);
   const bool norm = p.cfg.normalize, clamp = p.cfg.has_clamp;
   const int grid = (int)L.total_tiles;
-#define GF_FWD(N, C, O) render_fwd_kernel<NF, N, C, O><<<grid, kRenderThreads, 0, st>>>(p)
+#define GF_FWD(N, C, O)                                                                         \
+  do {                                                                                          \
+    if (fast32) render_fwd32_kernel<NF, N, C, O><<<grid, 32 * kFwd32Warps, 0, st>>>(p);         \
+    else render_fwd_kernel<NF, N, C, O><<<grid, kRenderThreads, 0, st>>>(p);                    \
+  } while (0)
+  const bool fast32 = cfg->tile_out == 32 && cfg->tile_in == 32;
   if (cfg->out_dtype == GF_F32) {
     if (norm) { if (clamp) GF_FWD(true, true, GF_F32); else GF_FWD(true, false, GF_F32); }
     else { if (clamp) GF_FWD(false, true, GF_F32); else GF_FWD(false, false, GF_F32); }
@@ -907,6 +1251,10 @@ gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout&
 
 template <int NF, bool N, bool C, int G>
 void launch_bwd_render(const Params<NF>& p, int grid, size_t smem, cudaStream_t st) {
+  if (p.cfg.tile_out == 32 && p.cfg.tile_in == 32) {
+    render_bwd32_kernel<NF, N, C, G><<<grid, 32 * kBwd32Warps, 0, st>>>(p);
+    return;
+  }
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(render_bwd_kernel<NF, N, C, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1070,7 +1418,12 @@ gf_status noalloc_launch(Params<NF>& p, const gf_config* cfg, const gf_batch* ba
   GF_LAUNCH_CHECK("bin_kernel");
   const bool norm = p.cfg.normalize, clamp = p.cfg.has_clamp;
   const int grid = (int)L.total_tiles;
-#define GF_FWD(N, C, O) render_fwd_kernel<NF, N, C, O><<<grid, kRenderThreads, 0, st>>>(p)
+#define GF_FWD(N, C, O)                                                                         \
+  do {                                                                                          \
+    if (fast32) render_fwd32_kernel<NF, N, C, O><<<grid, 32 * kFwd32Warps, 0, st>>>(p);         \
+    else render_fwd_kernel<NF, N, C, O><<<grid, kRenderThreads, 0, st>>>(p);                    \
+  } while (0)
+  const bool fast32 = cfg->tile_out == 32 && cfg->tile_in == 32;
   if (cfg->out_dtype == GF_F32) {
     if (norm) { if (clamp) GF_FWD(true, true, GF_F32); else GF_FWD(true, false, GF_F32); }
     else { if (clamp) GF_FWD(false, true, GF_F32); else GF_FWD(false, false, GF_F32); }
