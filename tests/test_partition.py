@@ -1,0 +1,75 @@
+"""Layer partition and the delta all-gather, on CPU gloo ranks (world size 2)."""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from guass_b200.partition import GatherLayout, all_gather_slots, field_costs, lpt_partition
+
+
+def test_field_costs_counts_element_evaluations():
+    # 40x70 field, 32x32 tiles: 2x3 tiles, edge tiles 8 rows / 6 cols
+    tp = [0, 2, 2, 3, 4, 4, 5]  # counts 2,0,1,1,0,1
+    cost = field_costs([tp], [(40, 70)])[0]
+    assert cost == 2 * 32 * 32 + 1 * 32 * 6 + 1 * 8 * 32 + 1 * 8 * 6
+
+
+def test_lpt_partition_balanced_and_deterministic():
+    costs = [100, 90, 80, 70, 60, 50, 40, 30, 20, 10]
+    parts = lpt_partition(costs, 3)
+    assert sorted(i for p in parts for i in p) == list(range(10))
+    loads = [sum(costs[i] for i in p) for p in parts]
+    assert max(loads) - min(loads) <= 20
+    assert parts == lpt_partition(costs, 3)
+    assert lpt_partition(costs, 1) == [list(range(10))]
+
+
+def test_gather_layout_offsets():
+    lay = GatherLayout([[0, 2], [1]], [10, 20, 30])
+    assert lay.owner == {0: 0, 2: 0, 1: 1}
+    assert lay.offset == {0: 0, 2: 10, 1: 0}
+    assert lay.rank_numel == [40, 20] and lay.slot == 64
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, numels, parts, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        lay = GatherLayout(parts, numels)
+        gathered = torch.zeros(world, lay.slot)
+        for f in parts[rank]:  # each rank "renders" its own fields
+            lay.field_view(gathered, f).fill_(float(f + 1))
+        all_gather_slots(gathered, rank)
+        ok = all(bool((lay.field_view(gathered, f) == f + 1).all()) for f in range(len(numels)))
+        q.put((rank, ok))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_all_gather_slots_on_gloo_ranks():
+    numels = [5, 7, 3, 9, 4]
+    parts = lpt_partition(numels, 2)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, numels, parts, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    res = dict(q.get(timeout=10) for _ in procs)
+    assert res == {0: True, 1: True}
+    assert all(p.exitcode == 0 for p in procs)
