@@ -10,7 +10,11 @@ import ctypes
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
-LIB_PATH = PKG / "libgfield.so"
+import os as _os
+
+# GUASS_B200_LIB points at another build of the same library (development
+# builds with different tuning); the default is the in-tree libgfield.so.
+LIB_PATH = Path(_os.environ["GUASS_B200_LIB"]) if _os.environ.get("GUASS_B200_LIB") else PKG / "libgfield.so"
 
 GF_ABI_VERSION = 1
 GF_MAX_FIELDS = 192

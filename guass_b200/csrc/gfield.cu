@@ -502,7 +502,10 @@ __device__ __forceinline__ f2 sub2(f2 a, f2 b) {
 // instructions in exactly the reference's association, expf and the
 // accumulation stay scalar and sequential: the fp32 output is bit-identical
 // to the generic kernel's and to the reference's.
-constexpr int kFwd32Warps = 2;
+#ifndef GF_FWD32_WARPS
+#define GF_FWD32_WARPS 2
+#endif
+constexpr int kFwd32Warps = GF_FWD32_WARPS;
 
 template <int NF, bool NORM, bool CLAMP, int OUTT>
 __global__ void __launch_bounds__(32 * kFwd32Warps)
@@ -823,10 +826,30 @@ render_bwd_kernel(const __grid_constant__ Params<NF> p) {
 // computed.  The six per-pair channels are reduced across the warp with a
 // reduce-scatter (9 shuffles instead of 30); lanes 0, 4, ..., 28 then hold
 // channels 0..7 and write the pair's slot with one 32-byte store.
-constexpr int kBwd32Warps = 4;
+#ifndef GF_BWD32_WARPS
+#define GF_BWD32_WARPS 4
+#endif
+#ifndef GF_BWD32_MINB
+#define GF_BWD32_MINB 0
+#endif
+#if GF_BWD32_MINB > 0
+#define GF_BWD32_BOUNDS __launch_bounds__(32 * GF_BWD32_WARPS, GF_BWD32_MINB)
+#else
+#define GF_BWD32_BOUNDS __launch_bounds__(32 * GF_BWD32_WARPS)
+#endif
+#ifndef GF_BWD32_SMEM_ROWS
+#define GF_BWD32_SMEM_ROWS 1
+#endif
+#ifndef GF_BWD32_PREFETCH
+#define GF_BWD32_PREFETCH 0
+#endif
+#ifndef GF_BWD32_SMEM_G
+#define GF_BWD32_SMEM_G 1
+#endif
+constexpr int kBwd32Warps = GF_BWD32_WARPS;
 
 template <int NF, bool NORM, bool CLAMP, int GT>
-__global__ void __launch_bounds__(32 * kBwd32Warps)
+__global__ void GF_BWD32_BOUNDS
 render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
   const int tg = blockIdx.x;
   const int fi = field_of_tile(p, tg);
@@ -843,22 +866,49 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
     return;
   }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (warp >= count) return;
   const int row0 = tr * 32, col0 = tc * 32;
   const int th = min(32, F.out_f - row0), tw = min(32, F.in_f - col0);
+#if GF_BWD32_SMEM_ROWS
+  __shared__ __align__(16) float s_rows[32];
+  if (threadIdx.x < 32) s_rows[threadIdx.x] = (threadIdx.x < th) ? F.row[row0 + threadIdx.x] : 0.0f;
+#endif
+#if GF_BWD32_SMEM_G
+  // dL/d(delta) tile, transposed: s_gt[col][row], row stride 34 floats so the
+  // per-lane 64-bit reads of two consecutive rows are bank-conflict free
+  __shared__ __align__(16) float s_gt[32 * 34];
+  for (int e = threadIdx.x; e < 1024; e += blockDim.x) {
+    const int r = e >> 5, c = e & 31;
+    s_gt[c * 34 + r] = (r < th && c < tw) ? load_grad<GT>(F.grad, (size_t)(row0 + r) * F.in_f + col0 + c) : 0.0f;
+  }
+#endif
+#if GF_BWD32_SMEM_ROWS || GF_BWD32_SMEM_G
+  __syncthreads();
+#endif
+  if (warp >= count) return;
   const bool cval = lane < tw;
   const float cc = cval ? F.col[col0 + lane] : 0.0f;
+#if !GF_BWD32_SMEM_ROWS
   const float myr = (lane < th) ? F.row[row0 + lane] : 0.0f;
-  f2 CR[16], G2[16];
+  f2 CR[16];
+#endif
+#if !GF_BWD32_SMEM_G
+  f2 G2[16];
+#endif
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
+#if !GF_BWD32_SMEM_ROWS
     CR[i] = pk2(__shfl_sync(0xffffffffu, myr, 2 * i), __shfl_sync(0xffffffffu, myr, 2 * i + 1));
+#endif
     const int r0 = 2 * i, r1 = 2 * i + 1;
     const size_t e0 = (size_t)(row0 + r0) * F.in_f + col0 + lane;
     const size_t e1 = (size_t)(row0 + r1) * F.in_f + col0 + lane;
+#if !GF_BWD32_SMEM_G
     const float g0 = (cval && r0 < th) ? load_grad<GT>(F.grad, e0) : 0.0f;
     const float g1 = (cval && r1 < th) ? load_grad<GT>(F.grad, e1) : 0.0f;
     G2[i] = pk2(g0, g1);
+#else
+    (void)r0; (void)r1; (void)e0; (void)e1;
+#endif
   }
   const int64_t* ids = ((p.batch_ids != nullptr) ? p.batch_ids : F.ids) + id_base + start;
   const float4* rec = p.records + 2 * (size_t)F.g_base;
@@ -868,9 +918,32 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
   const int my_ch = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
 
   int64_t gid = ids[warp];
+#if GF_BWD32_PREFETCH
+  // software pipeline: the box and record of the next pair are in flight
+  // while the current pair is computed
+  auto in_range = [&](int64_t g) { return g >= 0 && g < F.K; };
+  int4 nb = make_int4(0, -1, 0, -1);
+  float4 na = make_float4(0.f, 0.f, 0.f, 0.f), nh = na;
+  if (in_range(gid)) { nb = box[gid]; na = rec[2 * gid]; nh = rec[2 * gid + 1]; }
+  int64_t gid2 = (warp + kBwd32Warps < count) ? ids[warp + kBwd32Warps] : -1;
+#endif
   for (int64_t i = warp; i < count; i += kBwd32Warps) {
     const int64_t cur = gid;
     const int64_t prev = (i > 0) ? ids[i - 1] : -1;
+#if GF_BWD32_PREFETCH
+    int4 b = nb;
+    const float4 a = na;
+    const float4 h = nh;
+    gid = gid2;
+    if (i + kBwd32Warps < count && in_range(gid)) { nb = box[gid]; na = rec[2 * gid]; nh = rec[2 * gid + 1]; }
+    if (i + 2 * kBwd32Warps < count) gid2 = ids[i + 2 * kBwd32Warps];
+    bool ok = in_range(cur) && (prev < cur);
+    ok = ok && (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
+    if (!ok) {
+      if (lane == 0) atomicOr(p.status, GF_FLAG_STATE);
+      continue;
+    }
+#else
     if (i + kBwd32Warps < count) gid = ids[i + kBwd32Warps];
     bool ok = (cur >= 0) && (cur < F.K) && (prev < cur);
     int4 b = make_int4(0, -1, 0, -1);
@@ -884,6 +957,7 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
     }
     const float4 a = rec[2 * cur];
     const float4 h = rec[2 * cur + 1];
+#endif
     const float dy = cval ? __fsub_rn(cc, a.y) : 0.0f;
     const float a01 = __fmul_rn(h.y, dy);
     const float a11 = __fmul_rn(h.z, dy);
@@ -893,7 +967,12 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
     f2 T0 = zero2, U0 = zero2, U1 = zero2, U2 = zero2;
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
+#if GF_BWD32_SMEM_ROWS
+      const float2 rr = *reinterpret_cast<const float2*>(&s_rows[2 * k]);
+      const f2 DX = sub2(pk2(rr.x, rr.y), MUR);
+#else
       const f2 DX = sub2(CR[k], MUR);
+#endif
       const f2 T1 = fma2(H00, DX, A01);
       const f2 T2 = fma2(H01, DX, A11);
       const f2 Q = fma2(DX, T1, mul2(DY, T2));
@@ -913,7 +992,12 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
         e0 = __fmul_rn(e0, a.w);
         e1 = __fmul_rn(e1, a.w);
       }
+#if GF_BWD32_SMEM_G
+      const float2 gg = *reinterpret_cast<const float2*>(&s_gt[lane * 34 + 2 * k]);
+      const f2 GB = mul2(pk2(gg.x, gg.y), pk2(e0, e1));
+#else
       const f2 GB = mul2(G2[k], pk2(e0, e1));
+#endif
       T0 = add2(T0, GB);
       f2 GBA = GB;
       if (CLAMP) {
