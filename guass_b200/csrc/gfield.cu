@@ -818,39 +818,89 @@ render_bwd_kernel(const __grid_constant__ Params<NF> p) {
 
 // ---------------------------------------------------------------------------
 // Backward kernel 2, 32x32-tile fast path: one CTA of kBwd32Warps warps per
-// tile; warp w handles the tile's pairs w, w+W, ...  Every lane keeps its
-// column of dL/d(delta) (32 rows) and the 32 row coordinates in registers
-// for the whole tile, so the per-element loop touches no memory.  Row pairs
-// use packed fp32x2 arithmetic; the basis is evaluated exactly as in the
-// forward.  The next pair's id is fetched while the current pair is
-// computed.  The six per-pair channels are reduced across the warp with a
+// tile; warp w handles the tile's pairs w, w+W, ...  The tile's dL/d(delta)
+// is staged once in shared memory, transposed (s_gt[col][row], row stride 34
+// floats so each lane's 64-bit read of two consecutive rows is conflict
+// free), next to the 32 row coordinates.  Lane = column; rows go in pairs
+// through packed fp32x2 arithmetic; the basis is evaluated exactly as in the
+// forward.  The six per-pair channels are reduced across the warp with a
 // reduce-scatter (9 shuffles instead of 30); lanes 0, 4, ..., 28 then hold
 // channels 0..7 and write the pair's slot with one 32-byte store.
+//
+// Clamped elements (quad >= clamp_quad) lose their q-gradient
+// (backward.cu:318-321), which costs a max, a compare and a select per
+// element.  The quadratic form is convex, so over the tile it is largest at a
+// corner; when every corner is below the clamp by more than 1e-5 of the sum of
+// its absolute terms (about 20x the worst fp32 evaluation error of the element
+// formula), no element of the pair can be clamped and the loop without that
+// bookkeeping runs.  Results are identical either way.
 #ifndef GF_BWD32_WARPS
 #define GF_BWD32_WARPS 4
 #endif
-#ifndef GF_BWD32_MINB
-#define GF_BWD32_MINB 0
-#endif
-#if GF_BWD32_MINB > 0
-#define GF_BWD32_BOUNDS __launch_bounds__(32 * GF_BWD32_WARPS, GF_BWD32_MINB)
-#else
-#define GF_BWD32_BOUNDS __launch_bounds__(32 * GF_BWD32_WARPS)
-#endif
-#ifndef GF_BWD32_SMEM_ROWS
-#define GF_BWD32_SMEM_ROWS 1
-#endif
-#ifndef GF_BWD32_PREFETCH
-#define GF_BWD32_PREFETCH 0
-#endif
-#ifndef GF_BWD32_SMEM_G
-#define GF_BWD32_SMEM_G 1
-#endif
 constexpr int kBwd32Warps = GF_BWD32_WARPS;
 
+struct PairSums {
+  f2 T0, U0, U1, U2;
+};
+
+// Sum over the 32 rows of one lane's column for one pair.
+template <bool NORM, bool TRACK_CLAMP>
+__device__ __forceinline__ PairSums bwd32_pair_rows(const float* s_rows, const float* s_gcol, f2 H00, f2 H01,
+                                                   f2 A01, f2 A11, f2 DY, f2 MUR, float nclamp, float nf) {
+  const f2 zero2 = pk2(0.0f, 0.0f);
+  PairSums S{zero2, zero2, zero2, zero2};
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const float2 rr = *reinterpret_cast<const float2*>(&s_rows[2 * k]);
+    const f2 DX = sub2(pk2(rr.x, rr.y), MUR);
+    const f2 T1 = fma2(H00, DX, A01);
+    const f2 T2 = fma2(H01, DX, A11);
+    const f2 Q = fma2(DX, T1, mul2(DY, T2));
+    float q0, q1;
+    up2(Q, q0, q1);
+    q0 = fminf(q0, 0.0f);
+    q1 = fminf(q1, 0.0f);
+    bool act0 = true, act1 = true;
+    if (TRACK_CLAMP) {
+      act0 = q0 > nclamp;  // reference: quad < clamp
+      act1 = q1 > nclamp;
+      q0 = fmaxf(q0, nclamp);
+      q1 = fmaxf(q1, nclamp);
+    }
+    float e0 = expf(q0), e1 = expf(q1);
+    if (NORM) {
+      e0 = __fmul_rn(e0, nf);
+      e1 = __fmul_rn(e1, nf);
+    }
+    const float2 gg = *reinterpret_cast<const float2*>(&s_gcol[2 * k]);
+    const f2 GB = mul2(pk2(gg.x, gg.y), pk2(e0, e1));
+    S.T0 = add2(S.T0, GB);
+    f2 GBA = GB;
+    if (TRACK_CLAMP) {
+      float b0, b1;
+      up2(GB, b0, b1);
+      GBA = pk2(act0 ? b0 : 0.0f, act1 ? b1 : 0.0f);
+    }
+    S.U0 = add2(S.U0, GBA);
+    S.U1 = fma2(GBA, DX, S.U1);
+    S.U2 = fma2(mul2(GBA, DX), DX, S.U2);
+  }
+  return S;
+}
+
+// Lower bound of the scaled form q' = -0.5*quad at one tile corner, minus
+// the evaluation-error margin (h* are the -0.5-scaled inverse entries).
+__device__ __forceinline__ float corner_bound(float dx, float dy, float h00, float h01, float h11) {
+  const float q = dx * (h00 * dx + h01 * dy) + dy * (h01 * dx + h11 * dy);
+  const float s = fabsf(h00) * dx * dx + 2.0f * fabsf(h01) * fabsf(dx * dy) + fabsf(h11) * dy * dy;
+  return q - 1e-5f * s;
+}
+
 template <int NF, bool NORM, bool CLAMP, int GT>
-__global__ void GF_BWD32_BOUNDS
+__global__ void __launch_bounds__(32 * kBwd32Warps)
 render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
+  __shared__ __align__(16) float s_rows[32];
+  __shared__ __align__(16) float s_gt[32 * 34];
   const int tg = blockIdx.x;
   const int fi = field_of_tile(p, tg);
   const DevField& F = p.f[fi];
@@ -868,48 +918,18 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int row0 = tr * 32, col0 = tc * 32;
   const int th = min(32, F.out_f - row0), tw = min(32, F.in_f - col0);
-#if GF_BWD32_SMEM_ROWS
-  __shared__ __align__(16) float s_rows[32];
   if (threadIdx.x < 32) s_rows[threadIdx.x] = (threadIdx.x < th) ? F.row[row0 + threadIdx.x] : 0.0f;
-#endif
-#if GF_BWD32_SMEM_G
-  // dL/d(delta) tile, transposed: s_gt[col][row], row stride 34 floats so the
-  // per-lane 64-bit reads of two consecutive rows are bank-conflict free
-  __shared__ __align__(16) float s_gt[32 * 34];
   for (int e = threadIdx.x; e < 1024; e += blockDim.x) {
     const int r = e >> 5, c = e & 31;
     s_gt[c * 34 + r] = (r < th && c < tw) ? load_grad<GT>(F.grad, (size_t)(row0 + r) * F.in_f + col0 + c) : 0.0f;
   }
-#endif
-#if GF_BWD32_SMEM_ROWS || GF_BWD32_SMEM_G
   __syncthreads();
-#endif
   if (warp >= count) return;
   const bool cval = lane < tw;
   const float cc = cval ? F.col[col0 + lane] : 0.0f;
-#if !GF_BWD32_SMEM_ROWS
-  const float myr = (lane < th) ? F.row[row0 + lane] : 0.0f;
-  f2 CR[16];
-#endif
-#if !GF_BWD32_SMEM_G
-  f2 G2[16];
-#endif
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-#if !GF_BWD32_SMEM_ROWS
-    CR[i] = pk2(__shfl_sync(0xffffffffu, myr, 2 * i), __shfl_sync(0xffffffffu, myr, 2 * i + 1));
-#endif
-    const int r0 = 2 * i, r1 = 2 * i + 1;
-    const size_t e0 = (size_t)(row0 + r0) * F.in_f + col0 + lane;
-    const size_t e1 = (size_t)(row0 + r1) * F.in_f + col0 + lane;
-#if !GF_BWD32_SMEM_G
-    const float g0 = (cval && r0 < th) ? load_grad<GT>(F.grad, e0) : 0.0f;
-    const float g1 = (cval && r1 < th) ? load_grad<GT>(F.grad, e1) : 0.0f;
-    G2[i] = pk2(g0, g1);
-#else
-    (void)r0; (void)r1; (void)e0; (void)e1;
-#endif
-  }
+  const float c_first = F.col[col0], c_last = F.col[col0 + tw - 1];
+  const float r_first = s_rows[0], r_last = s_rows[th - 1];
+  const float* s_gcol = &s_gt[lane * 34];
   const int64_t* ids = ((p.batch_ids != nullptr) ? p.batch_ids : F.ids) + id_base + start;
   const float4* rec = p.records + 2 * (size_t)F.g_base;
   const int4* box = p.boxes + F.g_base;
@@ -918,32 +938,9 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
   const int my_ch = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
 
   int64_t gid = ids[warp];
-#if GF_BWD32_PREFETCH
-  // software pipeline: the box and record of the next pair are in flight
-  // while the current pair is computed
-  auto in_range = [&](int64_t g) { return g >= 0 && g < F.K; };
-  int4 nb = make_int4(0, -1, 0, -1);
-  float4 na = make_float4(0.f, 0.f, 0.f, 0.f), nh = na;
-  if (in_range(gid)) { nb = box[gid]; na = rec[2 * gid]; nh = rec[2 * gid + 1]; }
-  int64_t gid2 = (warp + kBwd32Warps < count) ? ids[warp + kBwd32Warps] : -1;
-#endif
   for (int64_t i = warp; i < count; i += kBwd32Warps) {
     const int64_t cur = gid;
     const int64_t prev = (i > 0) ? ids[i - 1] : -1;
-#if GF_BWD32_PREFETCH
-    int4 b = nb;
-    const float4 a = na;
-    const float4 h = nh;
-    gid = gid2;
-    if (i + kBwd32Warps < count && in_range(gid)) { nb = box[gid]; na = rec[2 * gid]; nh = rec[2 * gid + 1]; }
-    if (i + 2 * kBwd32Warps < count) gid2 = ids[i + 2 * kBwd32Warps];
-    bool ok = in_range(cur) && (prev < cur);
-    ok = ok && (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
-    if (!ok) {
-      if (lane == 0) atomicOr(p.status, GF_FLAG_STATE);
-      continue;
-    }
-#else
     if (i + kBwd32Warps < count) gid = ids[i + kBwd32Warps];
     bool ok = (cur >= 0) && (cur < F.K) && (prev < cur);
     int4 b = make_int4(0, -1, 0, -1);
@@ -957,63 +954,27 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
     }
     const float4 a = rec[2 * cur];
     const float4 h = rec[2 * cur + 1];
-#endif
     const float dy = cval ? __fsub_rn(cc, a.y) : 0.0f;
     const float a01 = __fmul_rn(h.y, dy);
     const float a11 = __fmul_rn(h.z, dy);
     const f2 H00 = pk2(h.x, h.x), H01 = pk2(h.y, h.y), A01 = pk2(a01, a01), A11 = pk2(a11, a11);
     const f2 DY = pk2(dy, dy), MUR = pk2(a.x, a.x);
-    const f2 zero2 = pk2(0.0f, 0.0f);
-    f2 T0 = zero2, U0 = zero2, U1 = zero2, U2 = zero2;
-#pragma unroll
-    for (int k = 0; k < 16; ++k) {
-#if GF_BWD32_SMEM_ROWS
-      const float2 rr = *reinterpret_cast<const float2*>(&s_rows[2 * k]);
-      const f2 DX = sub2(pk2(rr.x, rr.y), MUR);
-#else
-      const f2 DX = sub2(CR[k], MUR);
-#endif
-      const f2 T1 = fma2(H00, DX, A01);
-      const f2 T2 = fma2(H01, DX, A11);
-      const f2 Q = fma2(DX, T1, mul2(DY, T2));
-      float q0, q1;
-      up2(Q, q0, q1);
-      q0 = fminf(q0, 0.0f);
-      q1 = fminf(q1, 0.0f);
-      bool act0 = true, act1 = true;
-      if (CLAMP) {
-        act0 = q0 > nclamp;  // reference: quad < clamp
-        act1 = q1 > nclamp;
-        q0 = fmaxf(q0, nclamp);
-        q1 = fmaxf(q1, nclamp);
-      }
-      float e0 = expf(q0), e1 = expf(q1);
-      if (NORM) {
-        e0 = __fmul_rn(e0, a.w);
-        e1 = __fmul_rn(e1, a.w);
-      }
-#if GF_BWD32_SMEM_G
-      const float2 gg = *reinterpret_cast<const float2*>(&s_gt[lane * 34 + 2 * k]);
-      const f2 GB = mul2(pk2(gg.x, gg.y), pk2(e0, e1));
-#else
-      const f2 GB = mul2(G2[k], pk2(e0, e1));
-#endif
-      T0 = add2(T0, GB);
-      f2 GBA = GB;
-      if (CLAMP) {
-        float b0, b1;
-        up2(GB, b0, b1);
-        GBA = pk2(act0 ? b0 : 0.0f, act1 ? b1 : 0.0f);
-      }
-      U0 = add2(U0, GBA);
-      U1 = fma2(GBA, DX, U1);
-      U2 = fma2(mul2(GBA, DX), DX, U2);
+    bool track = CLAMP;
+    if (CLAMP) {
+      // warp-uniform: every lane evaluates the same four corners
+      const float dx0 = r_first - a.x, dx1 = r_last - a.x;
+      const float dy0 = c_first - a.y, dy1 = c_last - a.y;
+      const float lo = fminf(fminf(corner_bound(dx0, dy0, h.x, h.y, h.z), corner_bound(dx0, dy1, h.x, h.y, h.z)),
+                             fminf(corner_bound(dx1, dy0, h.x, h.y, h.z), corner_bound(dx1, dy1, h.x, h.y, h.z)));
+      track = !(lo > nclamp);
     }
+    PairSums S = track ? bwd32_pair_rows<NORM, true>(s_rows, s_gcol, H00, H01, A01, A11, DY, MUR, nclamp, a.w)
+                       : bwd32_pair_rows<NORM, false>(s_rows, s_gcol, H00, H01, A01, A11, DY, MUR, nclamp, a.w);
     float t0a, t0b, u0a, u0b, u1a, u1b, u2a, u2b;
-    up2(T0, t0a, t0b);
-    up2(U0, u0a, u0b);
-    up2(U1, u1a, u1b);
-    up2(U2, u2a, u2b);
+    up2(S.T0, t0a, t0b);
+    up2(S.U0, u0a, u0b);
+    up2(S.U1, u1a, u1b);
+    up2(S.U2, u2a, u2b);
     const float t0 = t0a + t0b, u0 = u0a + u0b, u1 = u1a + u1b, u2 = u2a + u2b;
     const float i00 = -2.0f * h.x, i01 = -2.0f * h.y, i11 = -2.0f * h.z;
     const float dyU0 = dy * u0;
