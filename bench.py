@@ -58,6 +58,9 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--exchange", choices=["auto", "multicast", "nccl"], default="auto",
+                    help="delta exchange for N > 1 (auto = nccl; multicast = NVLink multicast publish)")
+    ap.add_argument("--groups", type=int, default=4, help="forward field groups per rank (multicast exchange)")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
     return a
@@ -148,10 +151,10 @@ def sum_over_ranks(x: float, world: int) -> float:
 class UNetWorkload:
     """Fields of the whole UNet, partitioned; this rank's batch and buffers."""
 
-    def __init__(self, rank: int, world: int):
+    def __init__(self, rank: int, world: int, exchange: str = "auto", groups: int = 4):
         from guass_b200 import synthetic
         from guass_b200.batched import FieldBatch, pack_fields
-        from guass_b200.partition import GatherLayout, field_costs, lpt_partition
+        from guass_b200.partition import PartitionedRenderer, field_costs
 
         self.rank, self.world = rank, world
         self.fields = synthetic.cfg3()
@@ -169,27 +172,18 @@ class UNetWorkload:
         self.total_evals = sum(self.costs)
         self.total_pairs = full.total_pairs()
         del full, mu, chol, amp
-        self.parts = lpt_partition(self.costs, world)
-        self.layout = GatherLayout(self.parts, self.numels)
-        self.gathered = torch.zeros(world, self.layout.slot, dtype=torch.bfloat16, device="cuda")
-        own = self.parts[rank]
-        self.own = own
-        own_fields = [self.fields[i] for i in own]
+        use_mc = {"auto": False, "multicast": True, "nccl": False}[exchange]
+        self.renderer = PartitionedRenderer(shapes, self.costs, rank, world, groups=groups, use_multicast=use_mc)
+        self.parts, self.own = self.renderer.parts, self.renderer.own
+        self.layout, self.gathered = self.renderer.layout, self.renderer.gathered
+        own_fields = [self.fields[i] for i in self.own]
         self.mu, self.chol, self.amp, self.grad = pack_fields(own_fields, device="cuda")
-        self.batch = FieldBatch([shapes[i] for i in own],
-                                delta_out=self.gathered[rank, :self.layout.rank_numel[rank]])
-        while self.batch.ensure_capacity(self.mu, self.chol, self.amp):
-            pass
-        assert self.batch.device_flags() == 0
-        self.own_evals = sum(self.costs[i] for i in own)
+        self.renderer.ensure_capacity(self.mu, self.chol, self.amp)
+        assert self.renderer.device_flags() == 0
+        self.own_evals = sum(self.costs[i] for i in self.own)
 
     def step(self):
-        from guass_b200.partition import all_gather_slots
-
-        self.batch.forward(self.mu, self.chol, self.amp)
-        if self.world > 1:
-            all_gather_slots(self.gathered, self.rank)
-        self.batch.backward(self.grad, self.mu, self.chol, self.amp)
+        self.renderer.step(self.mu, self.chol, self.amp, self.grad)
 
 
 def run_device_timed(w: UNetWorkload, steps: int, warmup: int, world: int):
@@ -199,8 +193,10 @@ def run_device_timed(w: UNetWorkload, steps: int, warmup: int, world: int):
     for _ in range(warmup):
         w.step()
     torch.cuda.synchronize()
-    # 3 forward + 4 backward trace events per step (gfield.h, gf_trace_events)
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(7 * steps)]
+    # per step: 3 trace events per forward call, then 4 per backward call (gfield.h, gf_trace_events)
+    G = len(w.renderer.batches)
+    per_step = 7 * G
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(per_step * steps)]
     for e in evs:
         e.record()
     torch.cuda.synchronize()
@@ -209,6 +205,7 @@ def run_device_timed(w: UNetWorkload, steps: int, warmup: int, world: int):
     barrier(world)
     torch.cuda.synchronize()
     _lib.check(L.gf_trace_events(handles, len(evs)))
+    w.renderer.gather_events = [] if world > 1 else None
     start.record()
     for _ in range(steps):
         w.step()
@@ -219,19 +216,38 @@ def run_device_timed(w: UNetWorkload, steps: int, warmup: int, world: int):
     _lib.check(L.gf_trace_events(None, 0))
     assert recorded == len(evs), (recorded, len(evs))
     ms = start.elapsed_time(end) / steps
-    names = ("bin", "render_fwd", None, "bwd_prep", "render_bwd", "bwd_finalize")
-    per = {n: [] for n in names if n}
+    per = {n: [] for n in ("bin", "render_fwd", "bwd_prep", "render_bwd", "bwd_finalize")}
     for s in range(steps):
-        e = evs[7 * s: 7 * s + 7]
-        per["bin"].append(e[0].elapsed_time(e[1]))
-        per["render_fwd"].append(e[1].elapsed_time(e[2]))
-        per["bwd_prep"].append(e[3].elapsed_time(e[4]))
-        per["render_bwd"].append(e[4].elapsed_time(e[5]))
-        per["bwd_finalize"].append(e[5].elapsed_time(e[6]))
-        if world > 1:
-            per.setdefault("all_gather", []).append(e[2].elapsed_time(e[3]))
+        e = evs[per_step * s: per_step * (s + 1)]
+        b = 3 * G
+        per["bin"].append(sum(e[3 * g].elapsed_time(e[3 * g + 1]) for g in range(G)))
+        per["render_fwd"].append(sum(e[3 * g + 1].elapsed_time(e[3 * g + 2]) for g in range(G)))
+        per["bwd_prep"].append(sum(e[b + 4 * g].elapsed_time(e[b + 4 * g + 1]) for g in range(G)))
+        per["render_bwd"].append(sum(e[b + 4 * g + 1].elapsed_time(e[b + 4 * g + 2]) for g in range(G)))
+        per["bwd_finalize"].append(sum(e[b + 4 * g + 2].elapsed_time(e[b + 4 * g + 3]) for g in range(G)))
+    if world > 1:
+        per["exchange_side_stream"] = [a.elapsed_time(b) for a, b in w.renderer.gather_events]
+        w.renderer.gather_events = None
     kern = {k: sum(v) / len(v) for k, v in per.items()}
     return ms, kern
+
+
+def run_graph_timed(w: UNetWorkload, steps: int, warmup: int, world: int) -> float:
+    """The timed region: ``steps`` replays of the captured step."""
+    w.renderer.capture(w.mu, w.chol, w.amp, w.grad, warmup=2)
+    for _ in range(warmup):
+        w.renderer.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(steps):
+        w.renderer.replay()
+    end.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    return start.elapsed_time(end) / steps
 
 
 def run_e2e(w: UNetWorkload, steps: int, warmup: int, world: int):
@@ -371,13 +387,22 @@ def main():
         if world > 1:
             dist.destroy_process_group()
         return
-    w = UNetWorkload(rank, world)
+    w = UNetWorkload(rank, world, a.exchange, a.groups)
     sampler = ClockSampler() if local == 0 else None
     if sampler:
         sampler.start()
         time.sleep(0.3)
         sampler.mark("t0")
-    ms_local, kern = run_device_timed(w, a.steps, a.warmup, world)
+    if world == 1 or w.renderer.symm is not None:
+        # CUDA-graph replays (no NCCL inside the graph)
+        _, kern = run_device_timed(w, max(3, min(a.steps, 10)), a.warmup, world)
+        ms_local = run_graph_timed(w, a.steps, a.warmup, world)
+        timing = "value: CUDA-graph replays of the whole step; kernels_ms: eager steps with per-launch trace events"
+    else:
+        # NCCL collectives are never captured into a graph (a captured all-gather
+        # hung process teardown on this system); the step runs eagerly
+        ms_local, kern = run_device_timed(w, a.steps, a.warmup, world)
+        timing = "value and kernels_ms: eager steps (NCCL exchange) with per-launch trace events"
     if sampler:
         sampler.mark("t1")
     ms = max_over_ranks(ms_local, world)
@@ -421,10 +446,11 @@ def main():
                    "elements": w.total_elements, "pairs": w.total_pairs, "evals": w.total_evals,
                    "delta_dtype": "bf16", "grad_dtype": "f32", "tile": "32x32", "sigma_multiplier": 3.0,
                    "clamp_quad": 80.0, "partition": f"LPT by render cost over {world} rank(s)",
-                   "parallelism": f"layer-partition x{world} + NCCL all-gather of bf16 delta" if world > 1
-                   else "single GPU",
+                   "parallelism": f"layer-partition x{world} + {w.renderer.exchange} of bf16 delta "
+                                  f"({len(w.renderer.batches)} field groups)" if world > 1 else "single GPU",
                    "l2": "no flush: each step writes 187 MB of delta and reads 374 MB of dL/d(delta) (> 126 MB L2)"},
         "kernels_ms": kern_max,
+        "timing": timing,
         "roofline": {"kernel": dom, "bound": "fp32", "achieved": achieved, "peak": peak, "unit": "Tops/s",
                      "frac": achieved / peak,
                      "traffic": (traffic or {}).get("bytes_per_launch"),
@@ -437,7 +463,7 @@ def main():
         "clocks": clocks,
         "e2e": e2e,
         "cpu_baseline": cpu,
-        "gpu_launches": 5 * a.steps * world,
+        "gpu_launches": (5 * len(w.renderer.batches) + (len(w.renderer.batches) if w.renderer.symm is not None else 0)) * a.steps * world,
     }
     print(json.dumps(line), flush=True)
     if world > 1:

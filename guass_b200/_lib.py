@@ -41,7 +41,7 @@ GF_FLAG_INTERNAL = 0x4
 # Every symbol include/gfield.h declares.
 EXPORTED = ("gf_abi_version", "gf_last_error", "gf_num_tiles", "gf_workspace_bytes", "gf_forward",
             "gf_backward", "gf_workspace_status", "gf_trace_events", "gf_trace_count",
-            "gf_forward_noalloc")
+            "gf_forward_noalloc", "gf_multicast_store")
 
 
 class GfConfig(ctypes.Structure):
@@ -128,6 +128,8 @@ def lib() -> ctypes.CDLL:
     L.gf_trace_count.restype = ctypes.c_int
     L.gf_forward_noalloc.argtypes = [ctypes.POINTER(GfConfig), ctypes.POINTER(GfBatch), ctypes.c_void_p]
     L.gf_forward_noalloc.restype = ctypes.c_int
+    L.gf_multicast_store.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p]
+    L.gf_multicast_store.restype = ctypes.c_int
     if L.gf_abi_version() != GF_ABI_VERSION:
         raise ImportError(f"libgfield ABI {L.gf_abi_version()} != expected {GF_ABI_VERSION}")
     _lib = L

@@ -1426,6 +1426,41 @@ int gf_trace_count(void) { return gf::g_trace.used; }
 }  // extern "C"
 
 // ---------------------------------------------------------------------------
+// Multicast publish: each thread streams 16-byte chunks from local memory to
+// the NVLS multicast address (multimem.st); the switch replicates every store
+// to all GPUs bound to the multicast object.
+
+__global__ void multicast_store_kernel(const uint4* __restrict__ src, unsigned long long mc_dst, size_t n16) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n16; i += stride) {
+    const uint4 v = src[i];
+    const unsigned long long a = mc_dst + 16ull * i;
+    asm volatile("multimem.st.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(a), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
+  }
+  __threadfence_system();
+}
+
+extern "C" gf_status gf_multicast_store(const void* src, void* mc_dst, size_t bytes, int max_blocks,
+                                        gf_stream stream) {
+  if (bytes == 0) return GF_OK;
+  if (!src || !mc_dst) return gf::fail(GF_ERR_INVALID_ARG, "gf_multicast_store: src and mc_dst must be non-null");
+  if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(mc_dst) | bytes) & 15u)
+    return gf::fail(GF_ERR_INVALID_ARG, "gf_multicast_store: src, mc_dst and bytes must be multiples of 16");
+  if (max_blocks <= 0) return gf::fail(GF_ERR_INVALID_ARG, "gf_multicast_store: max_blocks must be positive");
+  const size_t n16 = bytes / 16;
+  const int threads = 512;
+  const size_t need = (n16 + threads - 1) / threads;
+  const int blocks = (int)(need < (size_t)max_blocks ? need : (size_t)max_blocks);
+  multicast_store_kernel<<<blocks, threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src), reinterpret_cast<unsigned long long>(mc_dst), n16);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return gf::fail(GF_ERR_CUDA, "gf_multicast_store: %s", cudaGetErrorString(e));
+  return GF_OK;
+}
+
+// ---------------------------------------------------------------------------
 // Forward render without caller scratch (gf_forward_noalloc).
 //
 // For callers that are handed their input and output buffers by a host that

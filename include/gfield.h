@@ -156,6 +156,17 @@ gf_status gf_workspace_status(void* workspace, gf_stream stream, int reset, uint
 gf_status gf_trace_events(void* const* events, int n);
 int gf_trace_count(void);
 
+/* Multi-GPU publish (no reference counterpart; GUASS has no layer
+ * partitioning).  Copies `bytes` from the local device buffer `src` to
+ * `mc_dst`, an NVLink multicast (NVLS) address of a buffer that every GPU of
+ * the group has mapped, with multimem stores: the NVSwitch delivers the data
+ * to every GPU's copy, so each GPU sends its share once.  Uses at most
+ * `max_blocks` CTAs (so it can run beside a render kernel), ends with a
+ * system-scope fence; the caller synchronises the group afterwards (for
+ * example with a symmetric-memory barrier) before reading peers' data.
+ * src, mc_dst and bytes must be multiples of 16. */
+gf_status gf_multicast_store(const void* src, void* mc_dst, size_t bytes, int max_blocks, gf_stream stream);
+
 /* Bytes of the library's static forward scratch (see gf_forward_noalloc). */
 #define GF_NOALLOC_SCRATCH_BYTES (4u << 20)
 
