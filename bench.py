@@ -381,12 +381,11 @@ def load_traffic(kernel: str):
 
 def main():
     a = parse_args()
-    rank, world, local = setup_dist()
     if a.impl == "reference":
-        reference_arm(a, rank, world)
-        if world > 1:
-            dist.destroy_process_group()
+        # host-only: no CUDA context, no process group; rank 0 alone works
+        reference_arm(a, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))
         return
+    rank, world, local = setup_dist()
     w = UNetWorkload(rank, world, a.exchange, a.groups)
     sampler = ClockSampler() if local == 0 else None
     if sampler:
