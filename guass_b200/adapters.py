@@ -1,0 +1,184 @@
+"""Whole-model use of the renderer: one batched render per step, flat gradients.
+
+The reference renders every ``GaussianLinear`` on its own, inside each layer's
+forward (gaussian_peft/layers/gaussian_linear.py:162-220, 235-242).  This
+module lets a model render all its adapters at once:
+
+* :class:`BatchedFieldFunction` -- autograd over a :class:`FieldBatch`: packed
+  ``(mu, chol_raw, amp)`` in, packed delta out; the backward is the batch's
+  exact backward.
+* :class:`BatchedAdapters` -- binds a model's Gaussian adapters (any module with
+  ``mu_raw``, ``chol_raw``, ``amp``, ``in_features``, ``out_features`` and an
+  ``adapter_config``, i.e. ``GaussianLinear``) to one batch.  ``render()`` packs
+  the module parameters (so they stay the parameters the optimizer, the
+  checkpoints and densify see), renders every delta in one launch set and
+  makes each module's ``compute_delta_weight()`` return its slice.
+* :func:`allreduce_adapter_grads` -- data parallelism: all adapter gradients of
+  the model in ONE flat all-reduce (the reference relies on DDP's bucketed
+  hooks over the same tensors, scripts/train_diffusion.py:87-91).
+* :func:`adapter_state_dict` / :func:`load_adapter_state_dict` -- the
+  reference's adapter checkpoint entries (gaussian_peft/checkpoints/
+  state_dict.py:12-44): per module ``mu_raw``, ``chol_raw``, ``amp``,
+  ``num_gaussians``, ``in_features``, ``out_features``, ``has_bias``.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+
+class BatchedFieldFunction(torch.autograd.Function):
+    """Packed render of every field of ``batch``.
+
+    ``batch`` provides ``forward(mu, chol_raw, amp) -> delta`` and
+    ``backward(grad, mu, chol_raw, amp) -> (d_mu, d_chol_raw, d_amp)``
+    (:class:`guass_b200.batched.FieldBatch`).  The returned delta is the
+    batch's own output buffer: it stays valid until the batch renders again."""
+
+    @staticmethod
+    def forward(ctx, batch, mu, chol_raw, amp):
+        mu, chol_raw, amp = mu.contiguous(), chol_raw.contiguous(), amp.contiguous()
+        delta = batch.forward(mu, chol_raw, amp)
+        ctx.batch = batch
+        ctx.save_for_backward(mu, chol_raw, amp)
+        return delta
+
+    @staticmethod
+    def backward(ctx, grad):
+        mu, chol_raw, amp = ctx.saved_tensors
+        batch = ctx.batch
+        want = getattr(batch, "grad_dtype", grad.dtype)
+        d_mu, d_chol, d_amp = batch.backward(grad.to(want).contiguous(), mu, chol_raw, amp)
+        return None, d_mu.clone(), d_chol.clone(), d_amp.clone()
+
+
+class BatchedAdapters:
+    """All Gaussian adapters of a model rendered by one batch per step.
+
+    ``modules`` maps names to adapter modules (``GaussianLinear``); their
+    shapes and K fix the batch, so after densify changes a K build a new
+    ``BatchedAdapters``.  ``batch_factory(shapes, **cfg)`` builds the batch
+    (default: :class:`~guass_b200.batched.FieldBatch` on the modules' device).
+    """
+
+    def __init__(self, modules: dict, batch_factory=None, out_dtype=torch.bfloat16):
+        self.names = list(modules)
+        self.modules = [modules[n] for n in self.names]
+        if not self.modules:
+            raise ValueError("no adapter modules")
+        cfg = self.modules[0].adapter_config
+        for m in self.modules:
+            c = m.adapter_config
+            if (c.tile_out, c.tile_in, c.sigma_multiplier, c.normalize_gaussian) != \
+                    (cfg.tile_out, cfg.tile_in, cfg.sigma_multiplier, cfg.normalize_gaussian):
+                raise ValueError("all adapters of one batch must share tile size, sigma and normalize")
+        self.shapes = [(m.out_features, m.in_features, int(m.mu_raw.shape[0])) for m in self.modules]
+        kw = dict(tile_out=cfg.tile_out, tile_in=cfg.tile_in, sigma_multiplier=cfg.sigma_multiplier,
+                  normalize=cfg.normalize_gaussian, clamp_quad=80.0,  # gaussian_linear.py:189
+                  out_dtype=out_dtype, grad_dtype=out_dtype)
+        if batch_factory is None:
+            from guass_b200.batched import FieldBatch
+
+            def batch_factory(shapes, **k):
+                return FieldBatch(shapes, device=self.modules[0].mu_raw.device, **k)
+        self.batch = batch_factory(self.shapes, **kw)
+        self.n_off = [0]
+        for o, i, _ in self.shapes:
+            self.n_off.append(self.n_off[-1] + o * i)
+        self._current = None
+        self._orig = {}
+
+    def render(self):
+        """Render every adapter's delta (autograd-connected) and return the
+        list of ``[out, in]`` deltas, already multiplied by adapter_scale."""
+        mu = torch.cat([torch.tanh(m.mu_raw) for m in self.modules])  # gaussian_linear.py:153-154
+        chol = torch.cat([m.chol_raw for m in self.modules])
+        amp = torch.cat([m.amp for m in self.modules])
+        packed = BatchedFieldFunction.apply(self.batch, mu, chol, amp)
+        out = []
+        for f, m in enumerate(self.modules):
+            d = packed[self.n_off[f]:self.n_off[f + 1]].view(m.out_features, m.in_features)
+            scale = m.adapter_config.adapter_scale
+            out.append(d * scale if scale != 1.0 else d)
+        self._current = out
+        return out
+
+    def install(self):
+        """Make each module's ``compute_delta_weight()`` return its slice of
+        the last :meth:`render` (call ``render()`` once per step before the
+        model's forward)."""
+        for f, m in enumerate(self.modules):
+            if id(m) in self._orig:
+                continue
+            self._orig[id(m)] = m.compute_delta_weight
+
+            def cdw(f=f):
+                if self._current is None:
+                    raise RuntimeError("BatchedAdapters.render() must run before the model's forward")
+                return self._current[f]
+
+            m.compute_delta_weight = cdw
+
+    def uninstall(self):
+        for m in self.modules:
+            orig = self._orig.pop(id(m), None)
+            if orig is not None:
+                m.compute_delta_weight = orig
+
+
+def adapter_parameters(modules) -> list[torch.Tensor]:
+    return [p for m in modules for p in (m.mu_raw, m.chol_raw, m.amp)]
+
+
+def allreduce_adapter_grads(modules, group=None, average: bool = True) -> None:
+    """Sum (and average) every adapter gradient across the group with one
+    flat all-reduce of the concatenated gradients."""
+    params = [p for p in adapter_parameters(modules) if p.grad is not None]
+    if not params:
+        return
+    flat = torch.cat([p.grad.reshape(-1) for p in params])
+    dist.all_reduce(flat, group=group)
+    if average:
+        flat /= dist.get_world_size(group)
+    off = 0
+    for p in params:
+        n = p.grad.numel()
+        p.grad.copy_(flat[off:off + n].view_as(p.grad))
+        off += n
+
+
+def adapter_state_dict(named_modules) -> dict:
+    """Reference adapter checkpoint entries for ``{name: module}``
+    (gaussian_peft/checkpoints/state_dict.py:12-26)."""
+    state = {}
+    for name, m in named_modules.items():
+        state[name] = {
+            "mu_raw": m.mu_raw.detach().cpu(),
+            "chol_raw": m.chol_raw.detach().cpu(),
+            "amp": m.amp.detach().cpu(),
+            "num_gaussians": int(m.mu_raw.shape[0]),
+            "in_features": m.in_features,
+            "out_features": m.out_features,
+            "has_bias": getattr(m, "bias", None) is not None,
+        }
+    return state
+
+
+def load_adapter_state_dict(named_modules, state: dict) -> None:
+    """Load reference adapter entries into ``{name: module}`` (schema-checked
+    like gaussian_peft/checkpoints/state_dict.py:29-84); K may differ from the
+    module's current K (densify), the parameters are replaced."""
+    for name, entry in state.items():
+        if name not in named_modules:
+            raise KeyError(f"Gaussian adapter target module {name!r} not found in model")
+        m = named_modules[name]
+        expected = {"in_features": m.in_features, "out_features": m.out_features,
+                    "has_bias": getattr(m, "bias", None) is not None}
+        actual = {k: entry[k] for k in expected}
+        if expected != actual:
+            raise ValueError(f"Adapter schema mismatch for {name!r}: expected {expected}, got {actual}")
+        dev, dt = m.mu_raw.device, m.mu_raw.dtype
+        m.mu_raw = nn.Parameter(entry["mu_raw"].to(dev, dt))
+        m.chol_raw = nn.Parameter(entry["chol_raw"].to(dev, dt))
+        m.amp = nn.Parameter(entry["amp"].to(dev, dt))

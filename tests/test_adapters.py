@@ -1,0 +1,209 @@
+"""Whole-model adapter plumbing (guass_b200.adapters), on the CPU.
+
+The batch is a test double computed with the CPU oracle, so these tests check
+the autograd wiring, the module binding, the flat gradient all-reduce (gloo
+ranks) and the checkpoint format -- not the CUDA kernels, which the GPU tests
+cover through the same FieldBatch interface.
+"""
+from __future__ import annotations
+
+import math
+import os
+import socket
+from dataclasses import dataclass
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+from torch import nn
+
+import oracle
+from guass_b200 import synthetic
+from guass_b200.adapters import (BatchedAdapters, adapter_state_dict, allreduce_adapter_grads,
+                                 load_adapter_state_dict)
+
+
+@dataclass
+class Cfg:
+    tile_out: int = 32
+    tile_in: int = 32
+    sigma_multiplier: float = 3.0
+    normalize_gaussian: bool = False
+    adapter_scale: float = 1.0
+
+
+class FakeLinear(nn.Module):
+    """The attributes of GaussianLinear that the binding uses."""
+
+    def __init__(self, out_f, in_f, k, seed, scale=1.0):
+        super().__init__()
+        f = synthetic.make_field(out_f, in_f, k, seed=seed, log_scale_mean=math.log(0.08))
+        self.out_features, self.in_features = out_f, in_f
+        self.mu_raw = nn.Parameter(torch.atanh(f.mu.clamp(-0.999, 0.999)))
+        self.chol_raw = nn.Parameter(f.chol_raw.clone())
+        self.amp = nn.Parameter(f.amp.clone())
+        self.row_coords, self.col_coords = f.row_coords, f.col_coords
+        self.adapter_config = Cfg(adapter_scale=scale)
+        self.bias = None
+
+    def compute_delta_weight(self):
+        raise AssertionError("the binding must replace this")
+
+
+class OracleBatch:
+    """FieldBatch interface computed with the CPU oracle."""
+
+    def __init__(self, shapes, **kw):
+        self.shapes = shapes
+        self.kw = dict(tile_out=kw["tile_out"], tile_in=kw["tile_in"], sigma_multiplier=kw["sigma_multiplier"],
+                       normalize=kw["normalize"], clamp_quad=kw["clamp_quad"])
+        self.grad_dtype = torch.float32
+        self.delta = torch.zeros(sum(o * i for o, i, _ in shapes))
+        self.calls = 0
+
+    def _axes(self, o, i):
+        return np.linspace(-1, 1, o, dtype=np.float32), np.linspace(-1, 1, i, dtype=np.float32)
+
+    def forward(self, mu, chol, amp):
+        self.calls += 1
+        off, g0, self.saved = 0, 0, []
+        for o, i, k in self.shapes:
+            r, c = self._axes(o, i)
+            d, tp, ids = oracle.forward(r, c, mu[g0:g0 + k].detach(), chol[g0:g0 + k].detach(),
+                                        amp[g0:g0 + k].detach(), **self.kw)
+            self.delta[off:off + o * i] = torch.from_numpy(d)
+            self.saved.append((tp, ids))
+            off += o * i
+            g0 += k
+        return self.delta
+
+    def backward(self, grad, mu, chol, amp):
+        outs, off, g0 = [], 0, 0
+        for (o, i, k), (tp, ids) in zip(self.shapes, self.saved):
+            r, c = self._axes(o, i)
+            outs.append(oracle.backward(grad[off:off + o * i].detach(), r, c, mu[g0:g0 + k].detach(),
+                                        chol[g0:g0 + k].detach(), amp[g0:g0 + k].detach(), tp, ids, **self.kw))
+            off += o * i
+            g0 += k
+        return tuple(torch.from_numpy(np.concatenate([x[j] for x in outs])) for j in range(3))
+
+
+def _modules():
+    return {"a": FakeLinear(40, 70, 6, 1), "b": FakeLinear(64, 32, 9, 2, scale=0.5), "c": FakeLinear(33, 40, 4, 3)}
+
+
+def test_render_matches_per_field_oracle_and_binds_modules():
+    mods = _modules()
+    bank = BatchedAdapters(mods, batch_factory=OracleBatch)
+    deltas = bank.render()
+    for (name, m), d in zip(mods.items(), deltas):
+        want, _, _ = oracle.forward(m.row_coords, m.col_coords, torch.tanh(m.mu_raw).detach(), m.chol_raw.detach(),
+                                    m.amp.detach())
+        assert torch.allclose(d, torch.from_numpy(want).view(m.out_features, m.in_features)
+                              * m.adapter_config.adapter_scale)
+    bank.install()
+    for m, d in zip(mods.values(), deltas):
+        assert m.compute_delta_weight() is d
+    bank.uninstall()
+    with pytest.raises(AssertionError):
+        mods["a"].compute_delta_weight()
+
+
+def test_gradients_reach_module_parameters():
+    mods = _modules()
+    bank = BatchedAdapters(mods, batch_factory=OracleBatch)
+    gs = [torch.randn(m.out_features, m.in_features, generator=torch.Generator().manual_seed(i))
+          for i, m in enumerate(mods.values())]
+    loss = sum((d * g).sum() for d, g in zip(bank.render(), gs))
+    loss.backward()
+    for m, g in zip(mods.values(), gs):
+        mu = torch.tanh(m.mu_raw).detach()
+        _, tp, ids = oracle.forward(m.row_coords, m.col_coords, mu, m.chol_raw.detach(), m.amp.detach())
+        d_mu, d_chol, d_amp = oracle.backward((g * m.adapter_config.adapter_scale).reshape(-1), m.row_coords,
+                                              m.col_coords, mu, m.chol_raw.detach(), m.amp.detach(), tp, ids)
+        assert torch.allclose(m.mu_raw.grad, torch.from_numpy(d_mu) * (1 - mu * mu), rtol=1e-5, atol=1e-9)
+        assert torch.allclose(m.chol_raw.grad, torch.from_numpy(d_chol), rtol=1e-5, atol=1e-9)
+        assert torch.allclose(m.amp.grad, torch.from_numpy(d_amp), rtol=1e-5, atol=1e-9)
+
+
+def test_mixed_render_settings_rejected():
+    mods = _modules()
+    mods["b"].adapter_config = Cfg(tile_out=16)
+    with pytest.raises(ValueError, match="share tile size"):
+        BatchedAdapters(mods, batch_factory=OracleBatch)
+
+
+def test_adapter_checkpoint_roundtrip_and_schema(tmp_path):
+    mods = _modules()
+    state = adapter_state_dict(mods)
+    assert set(state["a"]) == {"mu_raw", "chol_raw", "amp", "num_gaussians", "in_features", "out_features",
+                               "has_bias"}
+    path = tmp_path / "adapter.pt"
+    torch.save({"format": "gaussian-peft-adapter", "step": 3, "adapters": state}, path)
+    other = _modules()
+    for m in other.values():
+        with torch.no_grad():
+            m.amp.zero_()
+    load_adapter_state_dict(other, torch.load(path)["adapters"])
+    for n in mods:
+        assert torch.equal(other[n].amp, mods[n].amp) and torch.equal(other[n].mu_raw, mods[n].mu_raw)
+    bad = dict(state)
+    bad["a"] = dict(state["a"], in_features=71)
+    with pytest.raises(ValueError, match="schema mismatch"):
+        load_adapter_state_dict(other, bad)
+    with pytest.raises(KeyError):
+        load_adapter_state_dict(other, {"zzz": state["a"]})
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _dp_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        mods = _modules()
+        for m in mods.values():  # rank-dependent gradients
+            for p in (m.mu_raw, m.chol_raw, m.amp):
+                p.grad = torch.full_like(p, float(rank + 1))
+        allreduce_adapter_grads(mods.values())
+        ok = all(bool((p.grad == 1.5).all()) for m in mods.values() for p in (m.mu_raw, m.chol_raw, m.amp))
+        q.put((rank, ok))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_flat_allreduce_on_gloo_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert dict(q.get(timeout=10) for _ in procs) == {0: True, 1: True}
+
+
+def test_consecutive_steps_render_and_backward():
+    mods = _modules()
+    bank = BatchedAdapters(mods, batch_factory=OracleBatch)
+    opt = torch.optim.SGD([p for m in mods.values() for p in (m.mu_raw, m.chol_raw, m.amp)], lr=1e-3)
+    first = None
+    for step in range(2):
+        opt.zero_grad()
+        loss = sum(d.square().sum() for d in bank.render())
+        loss.backward()
+        g = mods["b"].amp.grad.clone()
+        if first is None:
+            first = g
+        opt.step()
+    assert bank.batch.calls == 2
+    assert not torch.equal(first, g)  # parameters moved, gradients follow
