@@ -1,0 +1,70 @@
+"""Integration with GUASS's own package (CPU; skipped where it is absent).
+
+The GPU box does not carry the reference, so these run in the build
+container only: they check that `guass_b200.cuda_field.install()` routes the
+reference runtime to this library, and that reference `GaussianLinear`
+layers served by `BatchedAdapters` give the reference's own output.
+"""
+from __future__ import annotations
+
+import sys
+
+import pytest
+import torch
+
+REF = "/root/reference"
+if REF not in sys.path:
+    sys.path.append(REF)
+gp = pytest.importorskip("gaussian_peft")
+
+from gaussian_peft.config.adapter import GaussianAdapterConfig  # noqa: E402
+from gaussian_peft.layers.gaussian_linear import GaussianLinear  # noqa: E402
+
+from test_adapters import OracleBatch  # noqa: E402
+
+from guass_b200 import cuda_field  # noqa: E402
+from guass_b200.adapters import BatchedAdapters, adapter_state_dict  # noqa: E402
+
+
+def test_install_routes_reference_runtime_to_this_library():
+    import gaussian_peft.cuda_field.loader as ref_loader
+    import gaussian_peft.cuda_field.runtime as ref_runtime
+
+    saved = (ref_loader.load_extension, ref_runtime.load_extension)
+    try:
+        cuda_field.install()
+        assert ref_runtime.load_extension is cuda_field.load_extension
+        ext = ref_runtime.load_extension()
+        assert type(ext).__module__ == "guass_b200.cuda_field._ext"
+        # the reference's train function now reaches our argument checks
+        args = dict(row_coords=torch.linspace(-1, 1, 8), col_coords=torch.linspace(-1, 1, 9), mu=torch.zeros(2, 2),
+                    chol_raw=torch.zeros(2, 3), amp=torch.zeros(2, 1), tile_out=32, tile_in=32, sigma_multiplier=3.0)
+        with pytest.raises(RuntimeError, match="row_coords must be a CUDA tensor"):
+            ref_runtime.gaussian_field_train(**args)
+    finally:
+        ref_loader.load_extension, ref_runtime.load_extension = saved
+
+
+def _layer(out_f, in_f, k, seed):
+    torch.manual_seed(seed)
+    cfg = GaussianAdapterConfig(init_num_gaussians=k, init_method="random_uniform", init_amp_scale=1e-2,
+                                execution_mode="tiled_reference_pytorch")
+    layer = GaussianLinear(in_f, out_f, adapter_config=cfg)
+    return layer
+
+
+def test_batched_adapters_serve_reference_layers():
+    layers = {"q": _layer(48, 64, 12, 0), "k": _layer(48, 40, 9, 1)}
+    x = torch.randn(3, 64), torch.randn(3, 40)
+    want = [layers["q"](x[0]), layers["k"](x[1])]  # reference path, per layer
+    bank = BatchedAdapters(layers, batch_factory=OracleBatch, out_dtype=torch.float32)
+    bank.install()
+    try:
+        bank.render()
+        got = [layers["q"](x[0]), layers["k"](x[1])]
+    finally:
+        bank.uninstall()
+    for a, b in zip(got, want):
+        assert torch.allclose(a, b, rtol=1e-4, atol=1e-6)
+    st = adapter_state_dict(layers)
+    assert st["q"]["num_gaussians"] == 12 and st["k"]["in_features"] == 40
