@@ -73,3 +73,37 @@ def test_all_gather_slots_on_gloo_ranks():
     res = dict(q.get(timeout=10) for _ in procs)
     assert res == {0: True, 1: True}
     assert all(p.exitcode == 0 for p in procs)
+
+
+def _dying_worker(rank, world, port, q):
+    import datetime
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    lay = GatherLayout([[0], [1]], [8, 8])
+    gathered = torch.zeros(world, lay.slot)
+    dist.barrier()
+    if rank == 1:
+        os._exit(0)  # the peer dies between steps, before the exchange
+    try:
+        all_gather_slots(gathered, rank)
+        q.put((rank, "completed"))
+    except Exception as exc:  # noqa: BLE001
+        q.put((rank, type(exc).__name__))
+
+
+def test_peer_death_surfaces_as_an_error():
+    """A rank that dies before the exchange makes the survivor's all-gather
+    fail with an exception within the process-group timeout, not hang."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dying_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    rank, outcome = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert rank == 0 and outcome != "completed"
