@@ -57,8 +57,9 @@ class BatchedAdapters:
     """All Gaussian adapters of a model rendered by one batch per step.
 
     ``modules`` maps names to adapter modules (``GaussianLinear``); their
-    shapes and K fix the batch, so after densify changes a K build a new
-    ``BatchedAdapters``.  ``batch_factory(shapes, **cfg)`` builds the batch
+    shapes and K fix the batch: after densify changes a K,
+    :meth:`shapes_changed` is true and :meth:`rebuilt` returns the binding for
+    the new K.  :meth:`freeze` / :meth:`merge_into_weights` serve inference.  ``batch_factory(shapes, **cfg)`` builds the batch
     (default: :class:`~guass_b200.batched.FieldBatch` on the modules' device).
     """
 
@@ -82,6 +83,7 @@ class BatchedAdapters:
 
             def batch_factory(shapes, **k):
                 return FieldBatch(shapes, device=self.modules[0].mu_raw.device, **k)
+        self._factory, self._out_dtype = batch_factory, out_dtype
         self.batch = batch_factory(self.shapes, **kw)
         self.n_off = [0]
         for o, i, _ in self.shapes:
@@ -89,9 +91,62 @@ class BatchedAdapters:
         self._current = None
         self._orig = {}
 
+    def shapes_changed(self) -> bool:
+        """True when a module's K differs from the batch's (densify cloned or
+        pruned Gaussians, gaussian_peft/trainers/base_trainer.py:127-220)."""
+        return any(int(m.mu_raw.shape[0]) != k for m, (_, _, k) in zip(self.modules, self.shapes))
+
+    def rebuilt(self) -> "BatchedAdapters":
+        """A new binding for the modules' current K (keeps install state)."""
+        fresh = BatchedAdapters(dict(zip(self.names, self.modules)), batch_factory=self._factory,
+                                out_dtype=self._out_dtype)
+        if self._orig:
+            self.uninstall()
+            fresh.install()
+        return fresh
+
+    @torch.no_grad()
+    def freeze(self):
+        """Inference: render once and serve the cached deltas until
+        :meth:`unfreeze` (the reference re-renders every layer at every
+        denoising step, scripts/sample_eval_10751.py:202-259)."""
+        self._frozen = False
+        self._frozen = [d.clone() for d in self.render()]
+        self._current = self._frozen
+        return self._frozen
+
+    def unfreeze(self):
+        self._frozen = None
+        self._current = None
+
+    @torch.no_grad()
+    def merge_into_weights(self):
+        """Inference: add each rendered delta into its module's base weight
+        once (in the weight's dtype) and make ``compute_delta_weight()``
+        return zeros, so the merged weight alone carries the adapter (for
+        export, or for a plain ``nn.Linear`` replacement).  Undo with
+        :meth:`unmerge_weights`."""
+        deltas = self.render()
+        self._merged = []
+        for m, d in zip(self.modules, deltas):
+            dw = d.to(m.weight.dtype)
+            m.weight.add_(dw)
+            self._merged.append(dw)
+        self._current = [torch.zeros_like(d) for d in deltas]
+        self.install()
+
+    @torch.no_grad()
+    def unmerge_weights(self):
+        for m, dw in zip(self.modules, getattr(self, "_merged", [])):
+            m.weight.sub_(dw)
+        self._merged = []
+        self._current = None
+
     def render(self):
         """Render every adapter's delta (autograd-connected) and return the
         list of ``[out, in]`` deltas, already multiplied by adapter_scale."""
+        if getattr(self, "_frozen", None):
+            return self._frozen
         mu = torch.cat([torch.tanh(m.mu_raw) for m in self.modules])  # gaussian_linear.py:153-154
         chol = torch.cat([m.chol_raw for m in self.modules])
         amp = torch.cat([m.amp for m in self.modules])

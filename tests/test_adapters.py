@@ -207,3 +207,34 @@ def test_consecutive_steps_render_and_backward():
         opt.step()
     assert bank.batch.calls == 2
     assert not torch.equal(first, g)  # parameters moved, gradients follow
+
+
+def test_freeze_serves_cached_render():
+    mods = _modules()
+    bank = BatchedAdapters(mods, batch_factory=OracleBatch)
+    bank.install()
+    frozen = bank.freeze()
+    calls = bank.batch.calls
+    for _ in range(3):  # e.g. denoising steps
+        assert all(torch.equal(m.compute_delta_weight(), d) for m, d in zip(mods.values(), frozen))
+        bank.render()
+    assert bank.batch.calls == calls
+    bank.unfreeze()
+    bank.render()
+    assert bank.batch.calls == calls + 1
+
+
+def test_densify_rebuild():
+    mods = _modules()
+    bank = BatchedAdapters(mods, batch_factory=OracleBatch)
+    bank.install()
+    assert not bank.shapes_changed()
+    m = mods["b"]  # clone two Gaussians, like densify
+    m.mu_raw = nn.Parameter(torch.cat([m.mu_raw.detach(), m.mu_raw.detach()[:2]]))
+    m.chol_raw = nn.Parameter(torch.cat([m.chol_raw.detach(), m.chol_raw.detach()[:2]]))
+    m.amp = nn.Parameter(torch.cat([m.amp.detach(), m.amp.detach()[:2]]))
+    assert bank.shapes_changed()
+    bank = bank.rebuilt()
+    assert bank.shapes[1][2] == 11 and not bank.shapes_changed()
+    deltas = bank.render()
+    assert torch.equal(mods["b"].compute_delta_weight(), deltas[1])

@@ -68,3 +68,19 @@ def test_batched_adapters_serve_reference_layers():
         assert torch.allclose(a, b, rtol=1e-4, atol=1e-6)
     st = adapter_state_dict(layers)
     assert st["q"]["num_gaussians"] == 12 and st["k"]["in_features"] == 40
+
+
+def test_merge_into_reference_weights():
+    layers = {"q": _layer(48, 64, 12, 0)}
+    x = torch.randn(3, 64)
+    want = layers["q"](x)
+    w0 = layers["q"].weight.detach().clone()
+    bank = BatchedAdapters(layers, batch_factory=OracleBatch, out_dtype=torch.float32)
+    bank.merge_into_weights()
+    try:
+        assert torch.allclose(layers["q"](x), want, rtol=1e-4, atol=1e-6)
+        assert not torch.equal(layers["q"].weight, w0)
+    finally:
+        bank.unmerge_weights()
+        bank.uninstall()
+    assert torch.allclose(layers["q"].weight, w0, atol=1e-7)
