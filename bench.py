@@ -12,9 +12,12 @@ work is fixed as N grows (strong scaling).
 
 Metric: delta elements rendered forward+backward per second, whole job.
 value  -- device time of the step, inputs resident in HBM (CUDA events, max over ranks)
-e2e    -- the same step through the drop-in per-layer API (guass_b200.cuda_field),
-          with parameters and dL/d(delta) copied from pinned host memory and the
-          gradients copied back, every step
+e2e    -- the same step through the whole-model API (guass_b200.batched /
+          partition) with this rank's packed parameters and dL/d(delta) copied
+          from pinned host memory and the packed gradients copied back, every
+          step
+e2e_dropin_per_layer -- the same, one call per layer through the drop-in API
+          (guass_b200.cuda_field), as GUASS's own layers would call it
 cpu_baseline / --impl reference -- the CPU oracle (a C restatement of the
           reference kernels, OpenMP over all host cores) on a bounded sample
 
