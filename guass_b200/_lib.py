@@ -16,7 +16,7 @@ import os as _os
 # builds with different tuning); the default is the in-tree libgfield.so.
 LIB_PATH = Path(_os.environ["GUASS_B200_LIB"]) if _os.environ.get("GUASS_B200_LIB") else PKG / "libgfield.so"
 
-GF_ABI_VERSION = 1
+GF_ABI_VERSION = 2
 GF_MAX_FIELDS = 192
 GF_NOALLOC_SCRATCH_BYTES = 4 << 20
 
@@ -76,6 +76,7 @@ class GfField(ctypes.Structure):
         ("d_mu", ctypes.c_void_p),
         ("d_chol_raw", ctypes.c_void_p),
         ("d_amp", ctypes.c_void_p),
+        ("base_weight", ctypes.c_void_p),
     ]
 
 

@@ -25,6 +25,7 @@ from __future__ import annotations
 
 import torch
 import torch.distributed as dist
+import torch.nn.functional as F
 from torch import nn
 
 
@@ -49,6 +50,9 @@ class BatchedFieldFunction(torch.autograd.Function):
         mu, chol_raw, amp = ctx.saved_tensors
         batch = ctx.batch
         want = getattr(batch, "grad_dtype", grad.dtype)
+        scale = getattr(batch, "out_scale", 1.0)  # delta = out_scale * value: dL/dvalue = scale * grad
+        if scale != 1.0:
+            grad = grad.float() * scale
         d_mu, d_chol, d_amp = batch.backward(grad.to(want).contiguous(), mu, chol_raw, amp)
         return None, d_mu.clone(), d_chol.clone(), d_amp.clone()
 
@@ -59,11 +63,20 @@ class BatchedAdapters:
     ``modules`` maps names to adapter modules (``GaussianLinear``); their
     shapes and K fix the batch: after densify changes a K,
     :meth:`shapes_changed` is true and :meth:`rebuilt` returns the binding for
-    the new K.  :meth:`freeze` / :meth:`merge_into_weights` serve inference.  ``batch_factory(shapes, **cfg)`` builds the batch
-    (default: :class:`~guass_b200.batched.FieldBatch` on the modules' device).
+    the new K.  :meth:`freeze` / :meth:`merge_into_weights` serve inference.
+    ``batch_factory(shapes, **cfg)`` builds the batch (default:
+    :class:`~guass_b200.batched.FieldBatch` on the modules' device).
+
+    ``fused_weight=True`` renders ``W_eff = W0 + adapter_scale * delta``
+    straight into one buffer (the renderer's fused-weight epilogue) and makes
+    each module's forward a single ``F.linear(x, W_eff, bias)``, replacing the
+    reference's base GEMM plus row-chunked delta GEMMs
+    (gaussian_peft/layers/gaussian_linear.py:222-242).  It needs frozen base
+    weights of ``out_dtype`` and one adapter_scale for all modules; call
+    :meth:`refresh_base` after changing a base weight.
     """
 
-    def __init__(self, modules: dict, batch_factory=None, out_dtype=torch.bfloat16):
+    def __init__(self, modules: dict, batch_factory=None, out_dtype=torch.bfloat16, fused_weight: bool = False):
         self.names = list(modules)
         self.modules = [modules[n] for n in self.names]
         if not self.modules:
@@ -78,6 +91,17 @@ class BatchedAdapters:
         kw = dict(tile_out=cfg.tile_out, tile_in=cfg.tile_in, sigma_multiplier=cfg.sigma_multiplier,
                   normalize=cfg.normalize_gaussian, clamp_quad=80.0,  # gaussian_linear.py:189
                   out_dtype=out_dtype, grad_dtype=out_dtype)
+        self.fused = bool(fused_weight)
+        self.w0 = None
+        if self.fused:
+            scales = {float(m.adapter_config.adapter_scale) for m in self.modules}
+            if len(scales) != 1:
+                raise ValueError("fused_weight needs one adapter_scale for all modules")
+            for m in self.modules:
+                if m.weight.dtype != out_dtype or m.weight.requires_grad:
+                    raise ValueError(f"fused_weight needs frozen base weights of {out_dtype}")
+            self.w0 = torch.cat([m.weight.detach().reshape(-1) for m in self.modules]).contiguous()
+            kw.update(out_scale=scales.pop(), base_weight=self.w0)
         if batch_factory is None:
             from guass_b200.batched import FieldBatch
 
@@ -91,6 +115,12 @@ class BatchedAdapters:
         self._current = None
         self._orig = {}
 
+    @torch.no_grad()
+    def refresh_base(self):
+        """Fused mode: copy the modules' current base weights into W0."""
+        if self.fused:
+            self.w0.copy_(torch.cat([m.weight.detach().reshape(-1) for m in self.modules]))
+
     def shapes_changed(self) -> bool:
         """True when a module's K differs from the batch's (densify cloned or
         pruned Gaussians, gaussian_peft/trainers/base_trainer.py:127-220)."""
@@ -99,7 +129,7 @@ class BatchedAdapters:
     def rebuilt(self) -> "BatchedAdapters":
         """A new binding for the modules' current K (keeps install state)."""
         fresh = BatchedAdapters(dict(zip(self.names, self.modules)), batch_factory=self._factory,
-                                out_dtype=self._out_dtype)
+                                out_dtype=self._out_dtype, fused_weight=self.fused)
         if self._orig:
             self.uninstall()
             fresh.install()
@@ -126,6 +156,8 @@ class BatchedAdapters:
         return zeros, so the merged weight alone carries the adapter (for
         export, or for a plain ``nn.Linear`` replacement).  Undo with
         :meth:`unmerge_weights`."""
+        if self.fused:
+            raise RuntimeError("merge_into_weights: the fused mode already applies W0 + delta")
         deltas = self.render()
         self._merged = []
         for m, d in zip(self.modules, deltas):
@@ -144,7 +176,8 @@ class BatchedAdapters:
 
     def render(self):
         """Render every adapter's delta (autograd-connected) and return the
-        list of ``[out, in]`` deltas, already multiplied by adapter_scale."""
+        list of ``[out, in]`` deltas, already multiplied by adapter_scale
+        (fused mode: the effective weights W0 + adapter_scale * delta)."""
         if getattr(self, "_frozen", None):
             return self._frozen
         mu = torch.cat([torch.tanh(m.mu_raw) for m in self.modules])  # gaussian_linear.py:153-154
@@ -155,23 +188,39 @@ class BatchedAdapters:
         for f, m in enumerate(self.modules):
             d = packed[self.n_off[f]:self.n_off[f + 1]].view(m.out_features, m.in_features)
             scale = m.adapter_config.adapter_scale
-            out.append(d * scale if scale != 1.0 else d)
+            out.append(d * scale if scale != 1.0 and not self.fused else d)
         self._current = out
         return out
+
+    def _slot(self, f):
+        if self._current is None:
+            raise RuntimeError("BatchedAdapters.render() must run before the model's forward")
+        return self._current[f]
 
     def install(self):
         """Make each module's ``compute_delta_weight()`` return its slice of
         the last :meth:`render` (call ``render()`` once per step before the
-        model's forward)."""
+        model's forward).  Fused mode: the module's forward becomes one
+        ``F.linear`` with its effective weight, and ``compute_delta_weight()``
+        returns ``W_eff - W0`` (for logging; off the hot path)."""
         for f, m in enumerate(self.modules):
             if id(m) in self._orig:
                 continue
-            self._orig[id(m)] = m.compute_delta_weight
+            self._orig[id(m)] = (m.compute_delta_weight, m.__dict__.get("forward"))
+            if self.fused:
+                n0, n1 = self.n_off[f], self.n_off[f + 1]
 
-            def cdw(f=f):
-                if self._current is None:
-                    raise RuntimeError("BatchedAdapters.render() must run before the model's forward")
-                return self._current[f]
+                def cdw(f=f, m=m, n0=n0, n1=n1):
+                    w0 = self.w0[n0:n1].view(m.out_features, m.in_features)
+                    return self._slot(f).float() - w0.float()
+
+                def fwd(x, f=f, m=m):
+                    return F.linear(x, self._slot(f), m.bias)
+
+                m.forward = fwd
+            else:
+                def cdw(f=f):
+                    return self._slot(f)
 
             m.compute_delta_weight = cdw
 
@@ -179,7 +228,11 @@ class BatchedAdapters:
         for m in self.modules:
             orig = self._orig.pop(id(m), None)
             if orig is not None:
-                m.compute_delta_weight = orig
+                m.compute_delta_weight = orig[0]
+                if orig[1] is None:
+                    m.__dict__.pop("forward", None)
+                else:
+                    m.forward = orig[1]
 
 
 def adapter_parameters(modules) -> list[torch.Tensor]:

@@ -12,6 +12,7 @@ Packed layout (all on one device):
   outputs     delta [sum out*in] (bf16 by default)                  (field f at n_off[f]:)
   binning     tile_ptr [sum (T+1)], ids [capacity], pair_base [n+1]
   gradients   d_mu, d_chol_raw, d_amp with the parameters' layout
+  base_weight optional [sum out*in] out_dtype: delta becomes W0 + out_scale*value
 The flat parameter/gradient layout is also what the data-parallel path
 all-reduces as one buffer.
 """
@@ -41,7 +42,8 @@ class FieldBatch:
     def __init__(self, shapes, *, tile_out: int = 32, tile_in: int = 32, sigma_multiplier: float = 3.0,
                  normalize: bool = False, clamp_quad: float | None = 80.0, out_dtype=torch.bfloat16,
                  grad_dtype=torch.float32, out_scale: float = 1.0, device="cuda", ids_capacity: int | None = None,
-                 row_coords=None, col_coords=None, delta_out: torch.Tensor | None = None):
+                 row_coords=None, col_coords=None, delta_out: torch.Tensor | None = None,
+                 base_weight: torch.Tensor | None = None):
         self.shapes = [s if isinstance(s, FieldShape) else FieldShape(*s) for s in shapes]
         n = len(self.shapes)
         if not 1 <= n <= _lib.GF_MAX_FIELDS:
@@ -52,6 +54,7 @@ class FieldBatch:
         self.device = dev
         self.tile_out, self.tile_in = int(tile_out), int(tile_in)
         self.out_dtype, self.grad_dtype = out_dtype, grad_dtype
+        self.out_scale = float(out_scale)
         self.cfg = make_config(tile_out, tile_in, sigma_multiplier, normalize, clamp_quad,
                                out_dtype=_DT[out_dtype], grad_dtype=_DT[grad_dtype], out_scale=out_scale)
         self._lib = _lib.lib()
@@ -91,6 +94,23 @@ class FieldBatch:
         self._grad_bound = None
         self._fields = (_lib.GfField * n)()
         self._batch = _lib.GfBatch(num_fields=n, fields=ctypes.cast(self._fields, ctypes.POINTER(_lib.GfField)))
+        self.base_weight = None
+        if base_weight is not None:
+            self.set_base_weight(base_weight)
+
+    def set_base_weight(self, base_weight: torch.Tensor | None) -> None:
+        """Fused weight: later forwards store ``W0 + out_scale * value`` (one
+        rounding to out_dtype) with W0 = ``base_weight`` (packed like delta;
+        it may be ``self.delta`` itself).  ``None`` restores the plain delta."""
+        if base_weight is not None:
+            if base_weight.dtype != self.out_dtype or not base_weight.is_contiguous() \
+                    or base_weight.numel() != self.numel() or base_weight.device != self.device:
+                raise ValueError(f"base_weight must be a contiguous {self.out_dtype} tensor of {self.numel()} "
+                                 f"elements on {self.device}")
+        self.base_weight = base_weight
+        esz = self.delta.element_size()
+        for f in range(len(self.shapes)):
+            self._fields[f].base_weight = None if base_weight is None else base_weight.data_ptr() + esz * self.n_off[f]
 
     # -- parameter helpers -------------------------------------------------
     def num_fields(self) -> int:

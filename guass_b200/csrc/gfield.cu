@@ -58,6 +58,7 @@ struct DevField {
   int64_t* tile_ptr;
   int64_t* ids;
   const void* grad;
+  const void* base;   // [out*in] out dtype or nullptr: forward stores base + value
   float* d_mu;
   float* d_chol;
   float* d_amp;
@@ -67,7 +68,7 @@ struct DevField {
   int32_t tile_base;  // first global tile index
   int32_t g_base;     // first global Gaussian index
   int32_t diff_base;  // first int of this field's global diff array
-  int32_t vec_ok;     // delta rows are 16-byte aligned for vector stores
+  int32_t vec_ok;     // delta (and base) rows are 16-byte aligned for vector access
   int32_t pad_;
 };
 
@@ -92,6 +93,8 @@ struct Params {
   int64_t* pair_base;    // [n+1] (shared-id mode)
   DevField f[NF];
 };
+// __grid_constant__ parameters are limited to 32764 bytes per launch.
+static_assert(sizeof(Params<GF_MAX_FIELDS>) <= 32764, "descriptor block exceeds the kernel-parameter limit");
 
 // ---------------------------------------------------------------------------
 // Geometry (forward.cu:134-209), bit-exact.
@@ -151,6 +154,32 @@ __device__ __forceinline__ Geo geometry(float mu_r, float mu_c, float raw11, flo
 // forward.cu:357-360: basis *= 1 / (2*pi*sqrt(max(det, floor)))
 __device__ __forceinline__ float norm_factor(float det) {
   return __fdiv_rn(1.0f, __fmul_rn((float)kTwoPi, __fsqrt_rn(fmaxf(det, kCovFloor))));
+}
+
+// Fused weight epilogue: with a base weight W0 the forward stores
+// out(float(W0[i]) + value[i]), one rounding to the output type, so a layer
+// can use W0 + delta as a single weight (one GEMM instead of the reference's
+// base GEMM plus row-chunked delta GEMMs, gaussian_linear.py:222-242).
+// `i` indexes the field's elements; value already carries out_scale.
+template <int OUTT>
+__device__ __forceinline__ float base_at(const void* b, size_t i) {
+  if (OUTT == GF_F32) return reinterpret_cast<const float*>(b)[i];
+  return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(b)[i]);
+}
+__device__ __forceinline__ float4 add_base4(const float* b, float4 x) {
+  const float4 w = *reinterpret_cast<const float4*>(b);
+  return make_float4(__fadd_rn(w.x, x.x), __fadd_rn(w.y, x.y), __fadd_rn(w.z, x.z), __fadd_rn(w.w, x.w));
+}
+// 8 bf16 of the base at b (16-byte aligned) added to x[0..7] in place.
+__device__ __forceinline__ void add_base8(const __nv_bfloat16* b, float* x) {
+  const uint4 u = *reinterpret_cast<const uint4*>(b);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
+    x[2 * k] = __fadd_rn(f.x, x[2 * k]);
+    x[2 * k + 1] = __fadd_rn(f.y, x[2 * k + 1]);
+  }
 }
 
 // Render-side record of one Gaussian: two float4.
@@ -423,12 +452,18 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
         float* out = reinterpret_cast<float*>(F.delta) + base;
         const int r = tid >> 3, q4 = (tid & 7) * 4;
         if (r < bh) {
+          const size_t o = (size_t)r * F.in_f + q4;
           if (F.vec_ok && q4 + 3 < bw) {
-            *reinterpret_cast<float4*>(out + (size_t)r * F.in_f + q4) =
-                make_float4(s_out[r][q4], s_out[r][q4 + 1], s_out[r][q4 + 2], s_out[r][q4 + 3]);
+            float4 x = make_float4(s_out[r][q4], s_out[r][q4 + 1], s_out[r][q4 + 2], s_out[r][q4 + 3]);
+            if (F.base) x = add_base4(reinterpret_cast<const float*>(F.base) + base + o, x);
+            *reinterpret_cast<float4*>(out + o) = x;
           } else {
             for (int k = 0; k < 4; ++k)
-              if (q4 + k < bw) out[(size_t)r * F.in_f + q4 + k] = s_out[r][q4 + k];
+              if (q4 + k < bw) {
+                float x = s_out[r][q4 + k];
+                if (F.base) x = __fadd_rn(base_at<GF_F32>(F.base, base + o + k), x);
+                out[o + k] = x;
+              }
           }
         }
       } else {
@@ -436,17 +471,26 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
         if (tid < 128) {
           const int r = tid >> 2, q8 = (tid & 3) * 8;
           if (r < bh) {
+            const size_t o = (size_t)r * F.in_f + q8;
             if (F.vec_ok && q8 + 7 < bw) {
+              float x[8];
+#pragma unroll
+              for (int k = 0; k < 8; ++k) x[k] = s_out[r][q8 + k];
+              if (F.base) add_base8(reinterpret_cast<const __nv_bfloat16*>(F.base) + base + o, x);
               uint32_t w[4];
 #pragma unroll
               for (int k = 0; k < 4; ++k) {
-                const __nv_bfloat162 h2 = __floats2bfloat162_rn(s_out[r][q8 + 2 * k], s_out[r][q8 + 2 * k + 1]);
+                const __nv_bfloat162 h2 = __floats2bfloat162_rn(x[2 * k], x[2 * k + 1]);
                 w[k] = *reinterpret_cast<const uint32_t*>(&h2);
               }
-              *reinterpret_cast<uint4*>(out + (size_t)r * F.in_f + q8) = make_uint4(w[0], w[1], w[2], w[3]);
+              *reinterpret_cast<uint4*>(out + o) = make_uint4(w[0], w[1], w[2], w[3]);
             } else {
               for (int k = 0; k < 8; ++k)
-                if (q8 + k < bw) out[(size_t)r * F.in_f + q8 + k] = __float2bfloat16_rn(s_out[r][q8 + k]);
+                if (q8 + k < bw) {
+                  float x = s_out[r][q8 + k];
+                  if (F.base) x = __fadd_rn(base_at<GF_BF16>(F.base, base + o + k), x);
+                  out[o + k] = __float2bfloat16_rn(x);
+                }
             }
           }
         }
@@ -610,12 +654,18 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
     for (int k = 0; k < R / 4; ++k) {
       const int r = k * 4 + (lane >> 3), q4 = (lane & 7) * 4;
       if (r < bh) {
+        const size_t o = (size_t)r * F.in_f + q4;
         if (F.vec_ok && q4 + 3 < tw) {
-          *reinterpret_cast<float4*>(out + (size_t)r * F.in_f + q4) =
-              *reinterpret_cast<const float4*>(&s_out[warp][r][q4]);
+          float4 x = *reinterpret_cast<const float4*>(&s_out[warp][r][q4]);
+          if (F.base) x = add_base4(reinterpret_cast<const float*>(F.base) + base + o, x);
+          *reinterpret_cast<float4*>(out + o) = x;
         } else {
           for (int j = 0; j < 4; ++j)
-            if (q4 + j < tw) out[(size_t)r * F.in_f + q4 + j] = s_out[warp][r][q4 + j];
+            if (q4 + j < tw) {
+              float x = s_out[warp][r][q4 + j];
+              if (F.base) x = __fadd_rn(base_at<GF_F32>(F.base, base + o + j), x);
+              out[o + j] = x;
+            }
         }
       }
     }
@@ -625,17 +675,28 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
     for (int k = 0; k < R / 8; ++k) {
       const int r = k * 8 + (lane >> 2), q8 = (lane & 3) * 8;
       if (r < bh) {
+        const size_t o = (size_t)r * F.in_f + q8;
         if (F.vec_ok && q8 + 7 < tw) {
-          const float4 x0 = *reinterpret_cast<const float4*>(&s_out[warp][r][q8]);
-          const float4 x1 = *reinterpret_cast<const float4*>(&s_out[warp][r][q8 + 4]);
+          float4 x0 = *reinterpret_cast<const float4*>(&s_out[warp][r][q8]);
+          float4 x1 = *reinterpret_cast<const float4*>(&s_out[warp][r][q8 + 4]);
+          if (F.base) {
+            float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            add_base8(reinterpret_cast<const __nv_bfloat16*>(F.base) + base + o, x);
+            x0 = make_float4(x[0], x[1], x[2], x[3]);
+            x1 = make_float4(x[4], x[5], x[6], x[7]);
+          }
           const __nv_bfloat162 h0 = __floats2bfloat162_rn(x0.x, x0.y), h1 = __floats2bfloat162_rn(x0.z, x0.w);
           const __nv_bfloat162 h2 = __floats2bfloat162_rn(x1.x, x1.y), h3 = __floats2bfloat162_rn(x1.z, x1.w);
-          *reinterpret_cast<uint4*>(out + (size_t)r * F.in_f + q8) =
+          *reinterpret_cast<uint4*>(out + o) =
               make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
                          *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3));
         } else {
           for (int j = 0; j < 8; ++j)
-            if (q8 + j < tw) out[(size_t)r * F.in_f + q8 + j] = __float2bfloat16_rn(s_out[warp][r][q8 + j]);
+            if (q8 + j < tw) {
+              float x = s_out[warp][r][q8 + j];
+              if (F.base) x = __fadd_rn(base_at<GF_BF16>(F.base, base + o + j), x);
+              out[o + j] = __float2bfloat16_rn(x);
+            }
         }
       }
     }
@@ -1224,6 +1285,7 @@ void fill_params(Params<NF>& P, const gf_config* cfg, const gf_batch* batch, con
     d.row = s.row_coords; d.col = s.col_coords; d.mu = s.mu; d.chol = s.chol_raw; d.amp = s.amp;
     d.delta = s.delta; d.tile_ptr = s.tile_ptr; d.ids = s.gaussian_ids; d.grad = s.grad_delta;
     d.d_mu = s.d_mu; d.d_chol = s.d_chol_raw; d.d_amp = s.d_amp;
+    d.base = s.base_weight;
     d.ids_cap = s.ids_capacity;
     d.part_base = part_base;
     if (!batch->ids) part_base += s.ids_capacity;
@@ -1240,7 +1302,8 @@ void fill_params(Params<NF>& P, const gf_config* cfg, const gf_batch* batch, con
     tile_base += d.ntr * d.ntc;
     g_base += d.K;
     const size_t vec = 16 / esz;
-    d.vec_ok = ((reinterpret_cast<uintptr_t>(s.delta) & 15u) == 0) && (s.in_features % (int64_t)vec == 0) &&
+    d.vec_ok = ((reinterpret_cast<uintptr_t>(s.delta) & 15u) == 0) &&
+               ((reinterpret_cast<uintptr_t>(s.base_weight) & 15u) == 0) && (s.in_features % (int64_t)vec == 0) &&
                (cfg->tile_in % (int64_t)vec == 0);
   }
 }

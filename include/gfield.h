@@ -41,7 +41,7 @@
 extern "C" {
 #endif
 
-#define GF_ABI_VERSION 1
+#define GF_ABI_VERSION 2
 /* Upper bound on fields per call (one kernel-parameter descriptor each). */
 #define GF_MAX_FIELDS 192
 
@@ -72,7 +72,8 @@ typedef struct gf_config {
   int32_t normalize;       /* multiply the basis by 1/(2*pi*sqrt(det)) */
   int32_t has_clamp_quad;  /* clamp the quadratic form at clamp_quad */
   double clamp_quad;
-  float out_scale;    /* delta is stored as out_scale * value (1.0 = reference) */
+  float out_scale;    /* delta is stored as out_scale * value (1.0 = reference);
+                         the backward takes dL/d(value), i.e. the caller scales */
   int32_t out_dtype;  /* gf_dtype of delta */
   int32_t grad_dtype; /* gf_dtype of grad_delta */
 } gf_config;
@@ -97,6 +98,14 @@ typedef struct gf_field {
   float* d_mu;             /* [K,2] (backward output) */
   float* d_chol_raw;       /* [K,3] (backward output) */
   float* d_amp;            /* [K]   (backward output) */
+  /* Optional fused weight (NULL = plain delta).  [out*in] of out_dtype; the
+   * forward then stores delta[i] = out_dtype(float(base_weight[i]) +
+   * out_scale * value[i]) with one rounding, i.e. W0 + delta for a layer
+   * that applies one weight instead of the reference's base + delta GEMMs
+   * (gaussian_peft/layers/gaussian_linear.py:222-242).  May equal `delta`
+   * (in place).  The backward is unchanged: grad_delta is dL/d(value),
+   * which for W_eff = W0 + out_scale * value is out_scale * dL/dW_eff. */
+  const void* base_weight;
 } gf_field;
 
 /* A batch of fields rendered by one set of launches.

@@ -53,7 +53,7 @@ int main(void) {
   printf("gf_field %zu\n", sizeof(gf_field));
   printf("gf_batch %zu\n", sizeof(gf_batch));
   F(gf_config, clamp_quad) F(gf_config, out_scale) F(gf_config, grad_dtype)
-  F(gf_field, row_coords) F(gf_field, ids_capacity) F(gf_field, d_amp)
+  F(gf_field, row_coords) F(gf_field, ids_capacity) F(gf_field, d_amp) F(gf_field, base_weight)
   F(gf_batch, fields) F(gf_batch, ids_capacity) F(gf_batch, pair_base)
   return 0;
 }

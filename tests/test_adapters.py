@@ -17,6 +17,7 @@ import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
+import torch.nn.functional as F
 from torch import nn
 
 import oracle
@@ -39,6 +40,8 @@ class FakeLinear(nn.Module):
 
     def __init__(self, out_f, in_f, k, seed, scale=1.0):
         super().__init__()
+        self.weight = nn.Parameter(torch.randn(out_f, in_f, generator=torch.Generator().manual_seed(seed)),
+                                   requires_grad=False)
         f = synthetic.make_field(out_f, in_f, k, seed=seed, log_scale_mean=math.log(0.08))
         self.out_features, self.in_features = out_f, in_f
         self.mu_raw = nn.Parameter(torch.atanh(f.mu.clamp(-0.999, 0.999)))
@@ -60,6 +63,8 @@ class OracleBatch:
         self.kw = dict(tile_out=kw["tile_out"], tile_in=kw["tile_in"], sigma_multiplier=kw["sigma_multiplier"],
                        normalize=kw["normalize"], clamp_quad=kw["clamp_quad"])
         self.grad_dtype = torch.float32
+        self.out_scale = float(kw.get("out_scale", 1.0))
+        self.base_weight = kw.get("base_weight")
         self.delta = torch.zeros(sum(o * i for o, i, _ in shapes))
         self.calls = 0
 
@@ -77,6 +82,10 @@ class OracleBatch:
             self.saved.append((tp, ids))
             off += o * i
             g0 += k
+        if self.out_scale != 1.0:
+            self.delta *= self.out_scale
+        if self.base_weight is not None:
+            self.delta += self.base_weight
         return self.delta
 
     def backward(self, grad, mu, chol, amp):
@@ -238,3 +247,54 @@ def test_densify_rebuild():
     assert bank.shapes[1][2] == 11 and not bank.shapes_changed()
     deltas = bank.render()
     assert torch.equal(mods["b"].compute_delta_weight(), deltas[1])
+
+
+def _grads(mods):
+    return [p.grad.clone() for m in mods.values() for p in (m.mu_raw, m.chol_raw, m.amp)]
+
+
+def test_fused_weight_equals_base_plus_delta_gemms():
+    """One GEMM with W0 + s*delta gives the reference layer's output
+    (F.linear(x, W0) + F.linear(x, s*delta), gaussian_linear.py:222-242) and
+    the same adapter gradients."""
+    def make():
+        return {"a": FakeLinear(40, 70, 6, 1, scale=0.5), "b": FakeLinear(64, 32, 9, 2, scale=0.5)}
+
+    gen = torch.Generator().manual_seed(3)
+    xs = {"a": torch.randn(5, 70, generator=gen), "b": torch.randn(5, 32, generator=gen)}
+    gys = {"a": torch.randn(5, 40, generator=gen), "b": torch.randn(5, 64, generator=gen)}
+
+    plain = make()
+    bank = BatchedAdapters(plain, batch_factory=OracleBatch, out_dtype=torch.float32)
+    bank.install()
+    bank.render()
+    ref_y = {n: F.linear(xs[n], m.weight) + F.linear(xs[n], m.compute_delta_weight()) for n, m in plain.items()}
+    sum((ref_y[n] * gys[n]).sum() for n in plain).backward()
+
+    fused = make()
+    fbank = BatchedAdapters(fused, batch_factory=OracleBatch, out_dtype=torch.float32, fused_weight=True)
+    fbank.install()
+    fbank.render()
+    y = {n: m(xs[n]) for n, m in fused.items()}
+    sum((y[n] * gys[n]).sum() for n in fused).backward()
+    for n in plain:
+        torch.testing.assert_close(y[n], ref_y[n], rtol=1e-5, atol=1e-6)
+        torch.testing.assert_close(fused[n].compute_delta_weight(), plain[n].compute_delta_weight().detach(),
+                                   rtol=0, atol=1e-6)  # W_eff - W0 keeps an ulp of |W0| <= ~4
+    for a, b in zip(_grads(fused), _grads(plain)):
+        torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-9)
+    fbank.uninstall()
+    with pytest.raises(NotImplementedError):
+        fused["a"](xs["a"])  # nn.Module's own forward is back (FakeLinear defines none)
+
+
+def test_fused_weight_requirements():
+    mods = _modules()
+    with pytest.raises(ValueError, match="one adapter_scale"):
+        BatchedAdapters(mods, batch_factory=OracleBatch, out_dtype=torch.float32, fused_weight=True)
+    mods = {"a": FakeLinear(40, 70, 6, 1)}
+    with pytest.raises(ValueError, match="frozen base weights"):
+        BatchedAdapters(mods, batch_factory=OracleBatch, out_dtype=torch.bfloat16, fused_weight=True)
+    mods["a"].weight.requires_grad_(True)
+    with pytest.raises(ValueError, match="frozen base weights"):
+        BatchedAdapters(mods, batch_factory=OracleBatch, out_dtype=torch.float32, fused_weight=True)
