@@ -41,7 +41,7 @@ GF_FLAG_INTERNAL = 0x4
 # Every symbol include/gfield.h declares.
 EXPORTED = ("gf_abi_version", "gf_last_error", "gf_num_tiles", "gf_workspace_bytes", "gf_forward",
             "gf_backward", "gf_workspace_status", "gf_trace_events", "gf_trace_count",
-            "gf_forward_noalloc", "gf_multicast_store")
+            "gf_forward_noalloc", "gf_multicast_store", "gf_grad_stats_accumulate")
 
 
 class GfConfig(ctypes.Structure):
@@ -93,6 +93,17 @@ class GfBatch(ctypes.Structure):
 _lib = None
 
 
+class GfStatsLayer(ctypes.Structure):
+    _fields_ = [
+        ("num_gaussians", ctypes.c_int64),
+        ("d_mu_raw", ctypes.c_void_p),
+        ("d_chol_raw", ctypes.c_void_p),
+        ("d_amp", ctypes.c_void_p),
+        ("amp", ctypes.c_void_p),
+        ("stats", ctypes.c_void_p),
+    ]
+
+
 class GfieldError(RuntimeError):
     """A libgfield call returned a non-OK status."""
 
@@ -131,6 +142,8 @@ def lib() -> ctypes.CDLL:
     L.gf_forward_noalloc.restype = ctypes.c_int
     L.gf_multicast_store.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p]
     L.gf_multicast_store.restype = ctypes.c_int
+    L.gf_grad_stats_accumulate.argtypes = [ctypes.c_int32, ctypes.POINTER(GfStatsLayer), ctypes.c_void_p]
+    L.gf_grad_stats_accumulate.restype = ctypes.c_int
     if L.gf_abi_version() != GF_ABI_VERSION:
         raise ImportError(f"libgfield ABI {L.gf_abi_version()} != expected {GF_ABI_VERSION}")
     _lib = L

@@ -1524,6 +1524,67 @@ extern "C" gf_status gf_multicast_store(const void* src, void* mc_dst, size_t by
 }
 
 // ---------------------------------------------------------------------------
+// Densify statistics (gf_grad_stats_accumulate): one thread per Gaussian, one
+// grid row per layer.  Each plane update is the reference's fp32 add_ of a
+// per-Gaussian score (controllers/stats.py:58-66).
+
+namespace gf {
+struct StatsParams {
+  int32_t n;
+  int32_t pad_;
+  gf_stats_layer l[GF_MAX_FIELDS];
+};
+static_assert(sizeof(StatsParams) <= 32764, "stats descriptor block exceeds the kernel-parameter limit");
+
+__global__ void __launch_bounds__(256) grad_stats_kernel(const __grid_constant__ StatsParams p) {
+  const gf_stats_layer& L = p.l[blockIdx.y];
+  const int64_t K = L.num_gaussians;
+  float* s = L.stats;
+  for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < K; k += (int64_t)gridDim.x * blockDim.x) {
+    if (L.d_mu_raw) {
+      const float a = L.d_mu_raw[2 * k], b = L.d_mu_raw[2 * k + 1];
+      s[k] = __fadd_rn(s[k], __fsqrt_rn(__fmaf_rn(b, b, __fmul_rn(a, a))));
+    }
+    if (L.d_chol_raw) {
+      const float a = L.d_chol_raw[3 * k], b = L.d_chol_raw[3 * k + 1], c = L.d_chol_raw[3 * k + 2];
+      s[K + k] = __fadd_rn(s[K + k], __fsqrt_rn(__fmaf_rn(c, c, __fmaf_rn(b, b, __fmul_rn(a, a)))));
+    }
+    if (L.d_amp) s[2 * K + k] = __fadd_rn(s[2 * K + k], fabsf(L.d_amp[k]));
+    if (L.amp) s[3 * K + k] = __fadd_rn(s[3 * K + k], fabsf(L.amp[k]));
+    s[4 * K + k] = __fadd_rn(s[4 * K + k], 1.0f);
+  }
+}
+}  // namespace gf
+
+extern "C" gf_status gf_grad_stats_accumulate(int32_t num_layers, const gf_stats_layer* layers, gf_stream stream) {
+  if (num_layers == 0) return GF_OK;
+  if (num_layers < 0 || num_layers > GF_MAX_FIELDS || !layers)
+    return gf::fail(GF_ERR_INVALID_ARG, "gf_grad_stats_accumulate: num_layers must be in 0..%d with a layer array",
+                    GF_MAX_FIELDS);
+  thread_local gf::StatsParams* tp = nullptr;
+  if (!tp) tp = new gf::StatsParams();
+  gf::StatsParams& p = *tp;
+  p.n = num_layers;
+  int64_t kmax = 0;
+  for (int i = 0; i < num_layers; ++i) {
+    const gf_stats_layer& L = layers[i];
+    if (L.num_gaussians < 0) return gf::fail(GF_ERR_INVALID_ARG, "gf_grad_stats_accumulate: layer %d: K < 0", i);
+    if (L.num_gaussians > 0 && !L.stats)
+      return gf::fail(GF_ERR_INVALID_ARG, "gf_grad_stats_accumulate: layer %d: stats must be non-null", i);
+    p.l[i] = L;
+    if (L.num_gaussians > kmax) kmax = L.num_gaussians;
+  }
+  if (kmax == 0) return GF_OK;
+  const int threads = 256;
+  const int64_t bx = (kmax + threads - 1) / threads;
+  const dim3 grid((unsigned)(bx < 64 ? bx : 64), (unsigned)num_layers);
+  gf::grad_stats_kernel<<<grid, threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return gf::fail(GF_ERR_CUDA, "gf_grad_stats_accumulate: %s", cudaGetErrorString(e));
+  return GF_OK;
+}
+
+// ---------------------------------------------------------------------------
 // Forward render without caller scratch (gf_forward_noalloc).
 //
 // For callers that are handed their input and output buffers by a host that

@@ -176,6 +176,25 @@ int gf_trace_count(void);
  * src, mc_dst and bytes must be multiples of 16. */
 gf_status gf_multicast_store(const void* src, void* mc_dst, size_t bytes, int max_blocks, gf_stream stream);
 
+/* Densify statistics of one layer, for gf_grad_stats_accumulate. */
+typedef struct gf_stats_layer {
+  int64_t num_gaussians;   /* K >= 0 */
+  const float* d_mu_raw;   /* [K,2] gradient of mu_raw, or NULL (adds nothing) */
+  const float* d_chol_raw; /* [K,3] gradient of chol_raw, or NULL */
+  const float* d_amp;      /* [K]   gradient of amp, or NULL */
+  const float* amp;        /* [K]   amplitudes, or NULL (contrib not updated) */
+  float* stats;            /* [5,K] planes: grad_mu, grad_cov, grad_amp, contrib, active_steps */
+} gf_stats_layer;
+
+/* One training step of GUASS's densify statistics for up to GF_MAX_FIELDS
+ * layers in one launch (GaussianStatsTracker.update_from_layer_grads,
+ * gaussian_peft/controllers/stats.py:47-66, which the reference runs as ~10
+ * tensor ops per layer): per Gaussian k
+ *   grad_mu += ||d_mu_raw[k]||_2, grad_cov += ||d_chol_raw[k]||_2,
+ *   grad_amp += |d_amp[k]|, contrib += |amp[k]|, active_steps += 1
+ * (stats.py:116-131).  `layers` is a HOST array read during the call. */
+gf_status gf_grad_stats_accumulate(int32_t num_layers, const gf_stats_layer* layers, gf_stream stream);
+
 /* Bytes of the library's static forward scratch (see gf_forward_noalloc). */
 #define GF_NOALLOC_SCRATCH_BYTES (4u << 20)
 

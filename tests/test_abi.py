@@ -52,9 +52,11 @@ int main(void) {
   printf("gf_config %zu\n", sizeof(gf_config));
   printf("gf_field %zu\n", sizeof(gf_field));
   printf("gf_batch %zu\n", sizeof(gf_batch));
+  printf("gf_stats_layer %zu\n", sizeof(gf_stats_layer));
   F(gf_config, clamp_quad) F(gf_config, out_scale) F(gf_config, grad_dtype)
   F(gf_field, row_coords) F(gf_field, ids_capacity) F(gf_field, d_amp) F(gf_field, base_weight)
   F(gf_batch, fields) F(gf_batch, ids_capacity) F(gf_batch, pair_base)
+  F(gf_stats_layer, d_mu_raw) F(gf_stats_layer, amp) F(gf_stats_layer, stats)
   return 0;
 }
 ''')
@@ -65,10 +67,12 @@ int main(void) {
     assert int(got["gf_config"]) == ctypes.sizeof(_lib.GfConfig)
     assert int(got["gf_field"]) == ctypes.sizeof(_lib.GfField)
     assert int(got["gf_batch"]) == ctypes.sizeof(_lib.GfBatch)
+    assert int(got["gf_stats_layer"]) == ctypes.sizeof(_lib.GfStatsLayer)
     for key, val in got.items():
         if "." in key:
             struct, member = key.split(".")
-            cls = {"gf_config": _lib.GfConfig, "gf_field": _lib.GfField, "gf_batch": _lib.GfBatch}[struct]
+            cls = {"gf_config": _lib.GfConfig, "gf_field": _lib.GfField, "gf_batch": _lib.GfBatch,
+                   "gf_stats_layer": _lib.GfStatsLayer}[struct]
             assert getattr(cls, member).offset == int(val), key
 
 
@@ -149,3 +153,20 @@ def test_shared_ids_requires_pair_base():
     b.ids = 1 << 20
     st = L.gf_forward(ctypes.byref(_cfg()), ctypes.byref(b), None, 0, None)
     assert st == _lib.GF_ERR_INVALID_ARG and "pair_base" in _lib.last_error()
+
+
+def test_grad_stats_argument_errors():
+    """Rejected on the host, before any device work."""
+    L = _lib.lib()
+    layers = (_lib.GfStatsLayer * 2)()
+    assert L.gf_grad_stats_accumulate(0, None, None) == _lib.GF_OK
+    assert L.gf_grad_stats_accumulate(-1, layers, None) == _lib.GF_ERR_INVALID_ARG
+    assert L.gf_grad_stats_accumulate(_lib.GF_MAX_FIELDS + 1, layers, None) == _lib.GF_ERR_INVALID_ARG
+    assert L.gf_grad_stats_accumulate(1, None, None) == _lib.GF_ERR_INVALID_ARG
+    layers[0].num_gaussians = 4  # stats missing
+    assert L.gf_grad_stats_accumulate(2, layers, None) == _lib.GF_ERR_INVALID_ARG
+    assert "stats must be non-null" in _lib.last_error()
+    layers[0].num_gaussians = -1
+    assert L.gf_grad_stats_accumulate(1, layers, None) == _lib.GF_ERR_INVALID_ARG
+    layers[0].num_gaussians = 0  # nothing to do: no launch
+    assert L.gf_grad_stats_accumulate(2, layers, None) == _lib.GF_OK
