@@ -25,9 +25,22 @@ def pytest_configure(config):
     oracle.build()
 
 
+# GPU modules run in this order (the others after them, test_zz_* last), so
+# that under -x the core parity tests always run before the newer ones.
+_GPU_ORDER = ("test_gpu_parity", "test_gpu_reference_ext", "test_gpu_properties", "test_gpu_multigpu")
+
+
+def _rank(item):
+    mod = item.module.__name__.rsplit(".", 1)[-1] if item.module else ""
+    if mod.startswith("test_zz"):
+        return len(_GPU_ORDER) + 1
+    return _GPU_ORDER.index(mod) if mod in _GPU_ORDER else len(_GPU_ORDER)
+
+
 def pytest_collection_modifyitems(config, items):
     import torch
 
+    items.sort(key=_rank)  # stable: file order within a rank
     if torch.cuda.is_available():
         return
     skip = pytest.mark.skip(reason="no CUDA device")
