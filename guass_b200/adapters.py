@@ -290,3 +290,86 @@ def load_adapter_state_dict(named_modules, state: dict) -> None:
         m.mu_raw = nn.Parameter(entry["mu_raw"].to(dev, dt))
         m.chol_raw = nn.Parameter(entry["chol_raw"].to(dev, dt))
         m.amp = nn.Parameter(entry["amp"].to(dev, dt))
+
+
+class CheckpointFields:
+    """A saved adapter checkpoint rendered without its model.
+
+    Takes the payload of the reference's ``save_adapter_checkpoint``
+    (gaussian_peft/checkpoints/io.py:18-32: ``{"format", "step", "metadata",
+    "adapters"}``) or just its ``adapters`` mapping, checks every entry like
+    ``load_gaussian_adapter_state_dict`` (checkpoints/state_dict.py:29-84,
+    shapes against ``num_gaussians``), and packs all modules into one batch:
+    ``mu = tanh(mu_raw)`` (gaussian_linear.py:153-154), ``chol_raw``, ``amp``.
+    Render settings come from ``metadata["adapter_config"]`` (tile_out,
+    tile_in, sigma_multiplier, normalize_gaussian, adapter_scale), else the
+    GaussianAdapterConfig defaults; keyword arguments override both.
+    ``render()`` returns ``{module name: [out, in] delta * adapter_scale}``,
+    or with ``base_weights`` the fused ``W0 + adapter_scale * delta``.
+    """
+
+    _DEFAULTS = dict(tile_out=32, tile_in=32, sigma_multiplier=3.0, normalize_gaussian=False, adapter_scale=1.0)
+
+    def __init__(self, checkpoint, device="cuda", out_dtype=torch.bfloat16, batch_factory=None,
+                 base_weights: dict | None = None, **overrides):
+        adapters = checkpoint.get("adapters", checkpoint) if isinstance(checkpoint, dict) else None
+        if not isinstance(adapters, dict) or not adapters:
+            raise ValueError("no adapter entries in the checkpoint")
+        meta = (checkpoint.get("metadata") or {}) if "adapters" in checkpoint else {}
+        cfg = dict(self._DEFAULTS)
+        cfg.update({k: v for k, v in (meta.get("adapter_config") or {}).items() if k in cfg})
+        unknown = set(overrides) - set(cfg)
+        if unknown:
+            raise TypeError(f"unknown render settings {sorted(unknown)}")
+        cfg.update(overrides)
+        self.config = cfg
+        self.names = list(adapters)
+        self.shapes, mus, chols, amps = [], [], [], []
+        for name in self.names:
+            e = adapters[name]
+            for key in ("mu_raw", "chol_raw", "amp", "num_gaussians", "in_features", "out_features"):
+                if key not in e:
+                    raise KeyError(f"adapter entry {name!r} has no {key!r}")
+            k = int(e["num_gaussians"])
+            for key, cols in (("mu_raw", 2), ("chol_raw", 3), ("amp", 1)):
+                t = e[key]
+                if not isinstance(t, torch.Tensor):
+                    raise TypeError(f"{name}.{key}: expected Tensor, got {type(t)!r}")
+                if t.shape[0] != k or t.numel() != k * cols:
+                    raise ValueError(f"{name}.{key}: shape {tuple(t.shape)} does not hold {k} Gaussians")
+            self.shapes.append((int(e["out_features"]), int(e["in_features"]), k))
+            mus.append(torch.tanh(e["mu_raw"].float().reshape(k, 2)))
+            chols.append(e["chol_raw"].float().reshape(k, 3))
+            amps.append(e["amp"].float().reshape(k, 1))
+        self.mu = torch.cat(mus).to(device).contiguous()
+        self.chol_raw = torch.cat(chols).to(device).contiguous()
+        self.amp = torch.cat(amps).to(device).contiguous()
+        self.n_off = [0]
+        for o, i, _ in self.shapes:
+            self.n_off.append(self.n_off[-1] + o * i)
+        kw = dict(tile_out=int(cfg["tile_out"]), tile_in=int(cfg["tile_in"]),
+                  sigma_multiplier=float(cfg["sigma_multiplier"]), normalize=bool(cfg["normalize_gaussian"]),
+                  clamp_quad=80.0, out_dtype=out_dtype, out_scale=float(cfg["adapter_scale"]))
+        if base_weights is not None:
+            missing = [n for n in self.names if n not in base_weights]
+            if missing:
+                raise KeyError(f"base_weights lacks {missing}")
+            w0 = []
+            for n, (o, i, _) in zip(self.names, self.shapes):
+                w = base_weights[n]
+                if tuple(w.shape) != (o, i):
+                    raise ValueError(f"base weight {n!r}: shape {tuple(w.shape)}, expected {(o, i)}")
+                w0.append(w.detach().to(device, out_dtype).reshape(-1))
+            kw["base_weight"] = torch.cat(w0).contiguous()
+        if batch_factory is None:
+            from guass_b200.batched import FieldBatch
+
+            def batch_factory(shapes, **k):
+                return FieldBatch(shapes, device=device, **k)
+        self.batch = batch_factory(self.shapes, **kw)
+
+    @torch.no_grad()
+    def render(self) -> dict:
+        packed = self.batch.forward(self.mu, self.chol_raw, self.amp)
+        return {n: packed[self.n_off[f]:self.n_off[f + 1]].view(o, i)
+                for f, (n, (o, i, _)) in enumerate(zip(self.names, self.shapes))}

@@ -22,7 +22,7 @@ from torch import nn
 
 import oracle
 from guass_b200 import synthetic
-from guass_b200.adapters import (BatchedAdapters, adapter_state_dict, allreduce_adapter_grads,
+from guass_b200.adapters import (BatchedAdapters, CheckpointFields, adapter_state_dict, allreduce_adapter_grads,
                                  load_adapter_state_dict)
 
 
@@ -298,3 +298,48 @@ def test_fused_weight_requirements():
     mods["a"].weight.requires_grad_(True)
     with pytest.raises(ValueError, match="frozen base weights"):
         BatchedAdapters(mods, batch_factory=OracleBatch, out_dtype=torch.float32, fused_weight=True)
+
+
+def test_checkpoint_renders_without_model(tmp_path):
+    mods = {"a": FakeLinear(40, 70, 6, 1, scale=0.5), "b": FakeLinear(64, 32, 9, 2, scale=0.5)}
+    payload = {"format": "gaussian-peft-adapter", "step": 7,
+               "metadata": {"adapter_config": {"adapter_scale": 0.5, "tile_out": 32, "tile_in": 32,
+                                               "sigma_multiplier": 3.0, "normalize_gaussian": False,
+                                               "init_method": "grid_overlap"}},
+               "adapters": adapter_state_dict(mods)}
+    path = tmp_path / "adapter.pt"
+    torch.save(payload, path)
+    loaded = torch.load(path, weights_only=False)
+    cf = CheckpointFields(loaded, device="cpu", out_dtype=torch.float32, batch_factory=OracleBatch)
+    assert cf.shapes == [(40, 70, 6), (64, 32, 9)] and cf.batch.out_scale == 0.5
+    want = {n: d.detach().clone() for n, d in
+            zip(mods, BatchedAdapters(mods, batch_factory=OracleBatch, out_dtype=torch.float32).render())}
+    got = {n: d.clone() for n, d in cf.render().items()}
+    for n in mods:
+        assert torch.equal(got[n], want[n])
+    # the adapters mapping alone works too (defaults: scale 1)
+    cf1 = CheckpointFields(loaded["adapters"], device="cpu", out_dtype=torch.float32, batch_factory=OracleBatch)
+    torch.testing.assert_close(cf1.render()["a"] * 0.5, want["a"], rtol=0, atol=0)
+    # fused base weights
+    w0 = {n: m.weight for n, m in mods.items()}
+    cff = CheckpointFields(loaded, device="cpu", out_dtype=torch.float32, batch_factory=OracleBatch, base_weights=w0)
+    for n, w in cff.render().items():
+        torch.testing.assert_close(w, mods[n].weight + want[n], rtol=0, atol=1e-6)
+
+
+def test_checkpoint_entries_checked():
+    mods = {"a": FakeLinear(40, 70, 6, 1)}
+    state = adapter_state_dict(mods)
+    bad = {"a": dict(state["a"], num_gaussians=7)}
+    with pytest.raises(ValueError, match="does not hold 7"):
+        CheckpointFields(bad, device="cpu", batch_factory=OracleBatch)
+    with pytest.raises(KeyError, match="amp"):
+        CheckpointFields({"a": {k: v for k, v in state["a"].items() if k != "amp"}}, device="cpu",
+                         batch_factory=OracleBatch)
+    with pytest.raises(TypeError, match="unknown render settings"):
+        CheckpointFields(state, device="cpu", batch_factory=OracleBatch, tile=16)
+    with pytest.raises(ValueError, match="no adapter entries"):
+        CheckpointFields({"format": "gaussian-peft-adapter", "adapters": {}}, device="cpu")
+    with pytest.raises(ValueError, match="base weight"):
+        CheckpointFields(state, device="cpu", batch_factory=OracleBatch, out_dtype=torch.float32,
+                         base_weights={"a": torch.zeros(3, 3)})

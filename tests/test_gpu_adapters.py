@@ -96,3 +96,18 @@ def test_freeze_and_merge_on_gpu():
         bank.unmerge_weights()
         for m, w in zip(mods.values(), w0):
             torch.testing.assert_close(m.weight, w, rtol=0, atol=1e-6)
+
+
+def test_checkpoint_fields_render_like_the_modules():
+    from guass_b200.adapters import CheckpointFields, adapter_state_dict
+
+    mods = {"q": _Adapter(320, 320, 64, 1, scale=0.5), "k": _Adapter(320, 768, 48, 2, scale=0.5)}
+    payload = {"format": "gaussian-peft-adapter", "metadata": {"adapter_config": {"adapter_scale": 0.5}},
+               "adapters": adapter_state_dict(mods)}
+    with torch.no_grad():
+        want = [d.clone() for d in BatchedAdapters(mods, out_dtype=torch.float32).render()]
+    cf = CheckpointFields(payload, device="cuda", out_dtype=torch.float32)
+    got = cf.render()
+    assert cf.batch.device_flags() == 0
+    for (name, m), w in zip(mods.items(), want):
+        assert torch.equal(got[name], w)  # out_scale in the kernel == fp32 multiply after it
