@@ -338,10 +338,10 @@ class CheckpointFields:
                 if t.shape[0] != k or t.numel() != k * cols:
                     raise ValueError(f"{name}.{key}: shape {tuple(t.shape)} does not hold {k} Gaussians")
             self.shapes.append((int(e["out_features"]), int(e["in_features"]), k))
-            mus.append(torch.tanh(e["mu_raw"].float().reshape(k, 2)))
+            mus.append(e["mu_raw"].float().reshape(k, 2))
             chols.append(e["chol_raw"].float().reshape(k, 3))
             amps.append(e["amp"].float().reshape(k, 1))
-        self.mu = torch.cat(mus).to(device).contiguous()
+        self.mu = torch.tanh(torch.cat(mus).to(device)).contiguous()  # on the device, as the layer does
         self.chol_raw = torch.cat(chols).to(device).contiguous()
         self.amp = torch.cat(amps).to(device).contiguous()
         self.n_off = [0]
