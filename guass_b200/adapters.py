@@ -29,6 +29,23 @@ import torch.nn.functional as F
 from torch import nn
 
 
+# Pair capacity: the exact upper bound (every Gaussian in every tile of its
+# field) costs 8 bytes of ids plus 32 bytes of backward partials per pair; up
+# to this many pairs (1.6 GB) it is reserved outright and no pair count can
+# overflow; an SD1.5 UNet with K=256 needs 23.4 M.  Larger batches measure
+# their pair count on the first render (and on ensure_capacity()).
+MAX_BOUND_PAIRS = 40_000_000
+
+
+def pair_bound(shapes, tile_out: int, tile_in: int) -> int:
+    return sum(k * -(-o // tile_out) * -(-i // tile_in) for o, i, k in shapes)
+
+
+def _capacity_kw(shapes, tile_out, tile_in):
+    bound = pair_bound(shapes, tile_out, tile_in)
+    return ({"ids_capacity": max(bound, 1)}, False) if bound <= MAX_BOUND_PAIRS else ({}, True)
+
+
 class BatchedFieldFunction(torch.autograd.Function):
     """Packed render of every field of ``batch``.
 
@@ -102,6 +119,8 @@ class BatchedAdapters:
                     raise ValueError(f"fused_weight needs frozen base weights of {out_dtype}")
             self.w0 = torch.cat([m.weight.detach().reshape(-1) for m in self.modules]).contiguous()
             kw.update(out_scale=scales.pop(), base_weight=self.w0)
+        cap_kw, self._measure = _capacity_kw(self.shapes, cfg.tile_out, cfg.tile_in)
+        kw.update(cap_kw)
         if batch_factory is None:
             from guass_b200.batched import FieldBatch
 
@@ -114,6 +133,23 @@ class BatchedAdapters:
             self.n_off.append(self.n_off[-1] + o * i)
         self._current = None
         self._orig = {}
+
+    def _packed_params(self):
+        mu = torch.cat([torch.tanh(m.mu_raw) for m in self.modules])  # gaussian_linear.py:153-154
+        chol = torch.cat([m.chol_raw for m in self.modules])
+        amp = torch.cat([m.amp for m in self.modules])
+        return mu, chol, amp
+
+    @torch.no_grad()
+    def ensure_capacity(self) -> None:
+        """Measure the current pair count and grow the id buffer to fit (one
+        host synchronisation).  Needed only for batches above MAX_BOUND_PAIRS,
+        whose capacity is not the exact bound: call it when the Gaussians may
+        have spread (after densify, every few hundred steps)."""
+        mu, chol, amp = (t.detach().contiguous() for t in self._packed_params())
+        while self.batch.ensure_capacity(mu, chol, amp):
+            pass
+        self._measure = False
 
     @torch.no_grad()
     def refresh_base(self):
@@ -180,9 +216,9 @@ class BatchedAdapters:
         (fused mode: the effective weights W0 + adapter_scale * delta)."""
         if getattr(self, "_frozen", None):
             return self._frozen
-        mu = torch.cat([torch.tanh(m.mu_raw) for m in self.modules])  # gaussian_linear.py:153-154
-        chol = torch.cat([m.chol_raw for m in self.modules])
-        amp = torch.cat([m.amp for m in self.modules])
+        if self._measure:
+            self.ensure_capacity()
+        mu, chol, amp = self._packed_params()
         packed = BatchedFieldFunction.apply(self.batch, mu, chol, amp)
         out = []
         for f, m in enumerate(self.modules):
@@ -350,6 +386,8 @@ class CheckpointFields:
         kw = dict(tile_out=int(cfg["tile_out"]), tile_in=int(cfg["tile_in"]),
                   sigma_multiplier=float(cfg["sigma_multiplier"]), normalize=bool(cfg["normalize_gaussian"]),
                   clamp_quad=80.0, out_dtype=out_dtype, out_scale=float(cfg["adapter_scale"]))
+        cap_kw, self._measure = _capacity_kw(self.shapes, kw["tile_out"], kw["tile_in"])
+        kw.update(cap_kw)
         if base_weights is not None:
             missing = [n for n in self.names if n not in base_weights]
             if missing:
@@ -370,6 +408,10 @@ class CheckpointFields:
 
     @torch.no_grad()
     def render(self) -> dict:
+        if self._measure:
+            while self.batch.ensure_capacity(self.mu, self.chol_raw, self.amp):
+                pass
+            self._measure = False
         packed = self.batch.forward(self.mu, self.chol_raw, self.amp)
         return {n: packed[self.n_off[f]:self.n_off[f + 1]].view(o, i)
                 for f, (n, (o, i, _)) in enumerate(zip(self.names, self.shapes))}

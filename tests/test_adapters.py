@@ -65,8 +65,14 @@ class OracleBatch:
         self.grad_dtype = torch.float32
         self.out_scale = float(kw.get("out_scale", 1.0))
         self.base_weight = kw.get("base_weight")
+        self.ids_capacity = kw.get("ids_capacity")
+        self.capacity_checks = 0
         self.delta = torch.zeros(sum(o * i for o, i, _ in shapes))
         self.calls = 0
+
+    def ensure_capacity(self, mu, chol, amp):
+        self.capacity_checks += 1
+        return False
 
     def _axes(self, o, i):
         return np.linspace(-1, 1, o, dtype=np.float32), np.linspace(-1, 1, i, dtype=np.float32)
@@ -343,3 +349,20 @@ def test_checkpoint_entries_checked():
     with pytest.raises(ValueError, match="base weight"):
         CheckpointFields(state, device="cpu", batch_factory=OracleBatch, out_dtype=torch.float32,
                          base_weights={"a": torch.zeros(3, 3)})
+
+
+def test_pair_capacity_bound_or_measured(monkeypatch):
+    import guass_b200.adapters as A
+
+    mods = _modules()
+    bank = BatchedAdapters(mods, batch_factory=OracleBatch)
+    # 40x70: 2x3 tiles, 64x32: 2x1, 33x40: 2x2 (32x32 tiles)
+    assert bank.batch.ids_capacity == 6 * 6 + 9 * 2 + 4 * 4
+    bank.render()
+    assert bank.batch.capacity_checks == 0
+    monkeypatch.setattr(A, "MAX_BOUND_PAIRS", 10)
+    bank = BatchedAdapters(mods, batch_factory=OracleBatch)
+    assert bank.batch.ids_capacity is None
+    bank.render()
+    bank.render()
+    assert bank.batch.capacity_checks == 1  # measured once, on the first render
