@@ -64,6 +64,12 @@ def parse_args():
     ap.add_argument("--exchange", choices=["auto", "multicast", "nccl"], default="auto",
                     help="delta exchange for N > 1 (auto = nccl; multicast = NVLink multicast publish)")
     ap.add_argument("--groups", type=int, default=4, help="forward field groups per rank (multicast exchange)")
+    ap.add_argument("--workload", choices=["cfg3", "cfg4"], default="cfg3",
+                    help="cfg3: whole-UNet batched render (default, the headline); cfg4: data-parallel "
+                         "SD1.5-UNet adapter training step")
+    ap.add_argument("--adapter-apply", choices=["fused", "reference"], default="fused",
+                    help="cfg4: one GEMM on W0+delta, or the reference layer's base GEMM + row-chunked delta GEMMs")
+    ap.add_argument("--batch", type=int, default=4, help="cfg4: samples per GPU")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
     return a
@@ -418,8 +424,148 @@ def load_traffic(kernel: str):
     return None
 
 
+# ---------------------------------------------------------------------------
+TRAIN_METRIC = "SD1.5-UNet Gaussian-adapter data-parallel training samples/s (128 projections, K=256)"
+
+
+def train_arm(a, rank: int, world: int, local: int) -> None:
+    """cfg4: one step = render every delta (batched), UNet forward + epsilon
+    MSE, backward (batched render backward), one flat NCCL all-reduce of the
+    Gaussian-parameter gradients, AdamW.  Weak scaling: a fixed batch per GPU."""
+    from guass_b200 import _lib, sd15
+    from guass_b200.adapters import BatchedAdapters
+    from guass_b200.partition import field_costs
+
+    L = _lib.lib()
+    cfg = sd15.UNetConfig()
+    torch.manual_seed(0)  # identical base weights on every rank
+    with torch.device("cuda"):
+        model = sd15.SD15UNet(cfg, dtype=torch.bfloat16)
+    model.cuda()
+    mods = model.adapters()
+    bank = BatchedAdapters(mods, out_dtype=torch.bfloat16, fused_weight=(a.adapter_apply == "fused"))
+    bank.install()
+    tr = sd15.DataParallelTrainer(model, bank, world=world)
+    inp = sd15.synthetic_inputs(cfg, a.batch, seed=1000 + rank, device="cuda")
+    host = [t.cpu().pin_memory() for t in inp.tensors()]
+    shapes = [(m.out_features, m.in_features) for m in mods.values()]
+
+    for _ in range(a.warmup):
+        tr.step(inp)
+    torch.cuda.synchronize()
+    assert bank.batch.device_flags() == 0
+    nf = len(shapes)
+    tps = [bank.batch.tile_ptr_view(i).cpu() for i in range(nf)]
+    evals = sum(field_costs(tps, shapes))
+    elements = sum(o * i for o, i in shapes)
+
+    sampler = ClockSampler() if local == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+        sampler.mark("t0")
+    # per step: 3 trace events in the render forward, 4 in its backward (gfield.h, gf_trace_events)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(7 * a.steps)]
+    for e in evs:
+        e.record()
+    torch.cuda.synchronize()
+    handles = (ctypes.c_void_p * len(evs))(*[e.cuda_event for e in evs])
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    _lib.check(L.gf_trace_events(handles, len(evs)))
+    start.record()
+    for _ in range(a.steps):
+        loss = tr.step(inp)
+    end.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    recorded = L.gf_trace_count()
+    _lib.check(L.gf_trace_events(None, 0))
+    if sampler:
+        sampler.mark("t1")
+    assert recorded == len(evs), (recorded, len(evs))
+    ms = max_over_ranks(start.elapsed_time(end) / a.steps, world)
+    per = {"render_fwd": [], "render_bwd": [], "render_total": []}
+    for st in range(a.steps):
+        e = evs[7 * st: 7 * (st + 1)]
+        per["render_fwd"].append(e[1].elapsed_time(e[2]))
+        per["render_bwd"].append(e[4].elapsed_time(e[5]))
+        per["render_total"].append(e[0].elapsed_time(e[2]) + e[3].elapsed_time(e[6]))
+    kern = {k: max_over_ranks(sum(v) / len(v), world) for k, v in per.items()}
+    clocks = sampler.stop() if sampler else None
+    assert torch.isfinite(loss).item()
+
+    # end to end: this step's inputs copied from pinned host memory, the loss read back, every step
+    d_in = inp.tensors()
+    h2d = sum(t.numel() * t.element_size() for t in host)
+
+    def e2e_step():
+        for h, d in zip(host, d_in):
+            d.copy_(h, non_blocking=True)
+        return tr.step(inp).cpu()
+
+    n_e2e = max(3, min(a.steps, 10))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n_e2e):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / n_e2e, world)
+
+    if rank == 0:
+        sm_count = torch.cuda.get_device_properties(0).multi_processor_count
+        f_mhz = (clocks or {}).get("sm_mhz") or 1965.0
+        achieved = evals * OPS_PER_EVAL["render_bwd"] / (kern["render_bwd"] / 1e3) / 1e12
+        peak = sm_count * SM_FP32_LANES * f_mhz * 1e6 / 1e12
+        samples = a.batch * world
+        line = {
+            "metric": TRAIN_METRIC, "value": samples / (ms / 1e3), "unit": "samples/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded latents/text/noise ~ N(0,1), t ~ U{0..999}; random-init SD1.5-shaped UNet)",
+            "config": {"workload": "cfg4 data-parallel adapter training step", "batch_per_gpu": a.batch,
+                       "latent": [cfg.latent_channels, cfg.latent_size, cfg.latent_size],
+                       "text": [cfg.text_tokens, cfg.cross_dim], "adapters": nf, "K": cfg.num_gaussians,
+                       "delta_elements": elements, "evals": evals, "adapter_apply": a.adapter_apply,
+                       "parallelism": f"dp{world}: flat NCCL all-reduce of Gaussian-parameter gradients"
+                       if world > 1 else "single GPU", "optimizer": "AdamW on mu_raw/chol_raw/amp",
+                       "l2": "no flush: the UNet step streams GBs of activations and weights"},
+            "kernels_ms": kern, "render_share": kern["render_total"] / ms,
+            "roofline": {"kernel": "render_bwd", "bound": "fp32", "achieved": achieved, "peak": peak,
+                         "unit": "Tops/s", "frac": achieved / peak, "traffic": None,
+                         "definition": "as the cfg3 line: 25 FMA-pipe ops per evaluation / CUDA-event launch time"},
+            "clocks": clocks,
+            "e2e": {"value": samples / (e2e_ms / 1e3), "unit": "samples/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": int(h2d * world), "d2h_bytes_per_step": 4 * world,
+                    "path": "DataParallelTrainer.step with latents/text/t/noise H2D from pinned memory "
+                            "and the loss read back, every step"},
+            "cpu_baseline": None,
+            "gpu_launches": 5 * a.steps * world,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     a = parse_args()
+    if a.impl == "reference" and a.workload == "cfg4":
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "cfg4 is a GPU training step of an SD1.5-sized "
+                              "UNet; the reference's CPU path would take minutes per step. Its layer composition "
+                              "is timed on the GPU with --adapter-apply reference"}), flush=True)
+        return
+    if a.workload == "cfg4":
+        rank, world, local = setup_dist()
+        train_arm(a, rank, world, local)
+        return
     if a.impl == "reference":
         # host-only: no CUDA context, no process group; rank 0 alone works
         reference_arm(a, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))

@@ -10,10 +10,10 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent.parent
 
 
-def _run(env_extra):
+def _run(env_extra, *extra):
     env = dict(os.environ, OMP_NUM_THREADS="4", **env_extra)
     out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1",
-                          "--warmup", "3"], capture_output=True, text=True, env=env, timeout=600, cwd=ROOT)
+                          "--warmup", "3", *extra], capture_output=True, text=True, env=env, timeout=600, cwd=ROOT)
     assert out.returncode == 0, out.stderr[-2000:]
     return [l for l in out.stdout.splitlines() if l.startswith("{")]
 
@@ -32,3 +32,11 @@ def test_reference_arm_line():
 
 def test_reference_arm_other_ranks_exit_quietly():
     assert _run({"RANK": "1", "WORLD_SIZE": "2"}) == []
+
+
+def test_reference_arm_training_workload_is_unavailable():
+    lines = _run({}, "--workload", "cfg4")
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and "unavailable" in d
+    assert _run({"RANK": "1", "WORLD_SIZE": "2"}, "--workload", "cfg4") == []
