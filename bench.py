@@ -61,8 +61,9 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--exchange", choices=["auto", "multicast", "nccl"], default="auto",
-                    help="delta exchange for N > 1 (auto = nccl; multicast = NVLink multicast publish)")
+    ap.add_argument("--exchange", choices=["auto", "multicast", "fused", "nccl"], default="auto",
+                    help="delta exchange for N > 1 (auto = nccl; multicast = NVLink multicast publish after each "
+                         "render group; fused = the render kernel stores through the multicast address)")
     ap.add_argument("--groups", type=int, default=4, help="forward field groups per rank (multicast exchange)")
     ap.add_argument("--workload", choices=["cfg3", "cfg4"], default="cfg3",
                     help="cfg3: whole-UNet batched render (default, the headline); cfg4: data-parallel "
@@ -181,8 +182,9 @@ class UNetWorkload:
         self.total_evals = sum(self.costs)
         self.total_pairs = full.total_pairs()
         del full, mu, chol, amp
-        use_mc = {"auto": False, "multicast": True, "nccl": False}[exchange]
-        self.renderer = PartitionedRenderer(shapes, self.costs, rank, world, groups=groups, use_multicast=use_mc)
+        use_mc = {"auto": False, "multicast": True, "fused": True, "nccl": False}[exchange]
+        self.renderer = PartitionedRenderer(shapes, self.costs, rank, world, groups=groups, use_multicast=use_mc,
+                                            fused=(exchange == "fused"))
         self.parts, self.own = self.renderer.parts, self.renderer.own
         self.layout, self.gathered = self.renderer.layout, self.renderer.gathered
         own_fields = [self.fields[i] for i in self.own]
@@ -228,6 +230,15 @@ def run_device_timed(w: UNetWorkload, steps: int, warmup: int, world: int):
     per = {n: [] for n in ("bin", "render_fwd", "bwd_prep", "render_bwd", "bwd_finalize")}
     for s in range(steps):
         e = evs[per_step * s: per_step * (s + 1)]
+        if w.renderer.fused:
+            # host call order: BIN stage (start, bin), backward on the side stream (start, prep,
+            # render, finalize), RENDER stage (render: from the end of binning, overlapping the backward)
+            per["bin"].append(e[0].elapsed_time(e[1]))
+            per["render_fwd"].append(e[1].elapsed_time(e[6]))
+            per["bwd_prep"].append(e[2].elapsed_time(e[3]))
+            per["render_bwd"].append(e[3].elapsed_time(e[4]))
+            per["bwd_finalize"].append(e[4].elapsed_time(e[5]))
+            continue
         b = 3 * G
         per["bin"].append(sum(e[3 * g].elapsed_time(e[3 * g + 1]) for g in range(G)))
         per["render_fwd"].append(sum(e[3 * g + 1].elapsed_time(e[3 * g + 2]) for g in range(G)))

@@ -34,6 +34,8 @@ GF_BF16 = 1
 GF_PASS_FORWARD = 0
 GF_PASS_BACKWARD = 1
 
+GF_STAGE_BIN = 1
+GF_STAGE_RENDER = 2
 GF_FLAG_CAPACITY = 0x1
 GF_FLAG_STATE = 0x2
 GF_FLAG_INTERNAL = 0x4
@@ -41,7 +43,8 @@ GF_FLAG_INTERNAL = 0x4
 # Every symbol include/gfield.h declares.
 EXPORTED = ("gf_abi_version", "gf_last_error", "gf_num_tiles", "gf_workspace_bytes", "gf_forward",
             "gf_backward", "gf_workspace_status", "gf_trace_events", "gf_trace_count",
-            "gf_forward_noalloc", "gf_multicast_store", "gf_grad_stats_accumulate")
+            "gf_forward_noalloc", "gf_multicast_store", "gf_grad_stats_accumulate",
+            "gf_forward_stages")
 
 
 class GfConfig(ctypes.Structure):
@@ -77,6 +80,7 @@ class GfField(ctypes.Structure):
         ("d_chol_raw", ctypes.c_void_p),
         ("d_amp", ctypes.c_void_p),
         ("base_weight", ctypes.c_void_p),
+        ("delta_multicast", ctypes.c_void_p),
     ]
 
 
@@ -144,6 +148,9 @@ def lib() -> ctypes.CDLL:
     L.gf_multicast_store.restype = ctypes.c_int
     L.gf_grad_stats_accumulate.argtypes = [ctypes.c_int32, ctypes.POINTER(GfStatsLayer), ctypes.c_void_p]
     L.gf_grad_stats_accumulate.restype = ctypes.c_int
+    L.gf_forward_stages.argtypes = [ctypes.POINTER(GfConfig), ctypes.POINTER(GfBatch), ctypes.c_void_p,
+                                    ctypes.c_size_t, ctypes.c_uint, ctypes.c_void_p]
+    L.gf_forward_stages.restype = ctypes.c_int
     if L.gf_abi_version() != GF_ABI_VERSION:
         raise ImportError(f"libgfield ABI {L.gf_abi_version()} != expected {GF_ABI_VERSION}")
     _lib = L

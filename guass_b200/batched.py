@@ -43,7 +43,7 @@ class FieldBatch:
                  normalize: bool = False, clamp_quad: float | None = 80.0, out_dtype=torch.bfloat16,
                  grad_dtype=torch.float32, out_scale: float = 1.0, device="cuda", ids_capacity: int | None = None,
                  row_coords=None, col_coords=None, delta_out: torch.Tensor | None = None,
-                 base_weight: torch.Tensor | None = None):
+                 base_weight: torch.Tensor | None = None, delta_multicast: int | None = None):
         self.shapes = [s if isinstance(s, FieldShape) else FieldShape(*s) for s in shapes]
         n = len(self.shapes)
         if not 1 <= n <= _lib.GF_MAX_FIELDS:
@@ -89,7 +89,8 @@ class FieldBatch:
         self.d_mu = torch.empty(total_g, 2, dtype=torch.float32, device=dev)
         self.d_chol_raw = torch.empty(total_g, 3, dtype=torch.float32, device=dev)
         self.d_amp = torch.empty(total_g, 1, dtype=torch.float32, device=dev)
-        self._ws = None
+        self._ws = None      # forward workspace
+        self._ws_bwd = None  # backward workspace (separate, so a backward may overlap a render)
         self._bound = None
         self._grad_bound = None
         self._fields = (_lib.GfField * n)()
@@ -97,6 +98,20 @@ class FieldBatch:
         self.base_weight = None
         if base_weight is not None:
             self.set_base_weight(base_weight)
+        self.delta_multicast = None
+        if delta_multicast:
+            self.set_delta_multicast(delta_multicast)
+
+    def set_delta_multicast(self, address: int | None) -> None:
+        """Render through NVLink multicast: ``address`` is the multicast (NVLS)
+        address of ``self.delta``'s first element; every forward then writes
+        the delta of every GPU bound to that multicast object (the render and
+        the all-gather in one kernel).  The caller runs a group barrier before
+        any GPU reads the result.  ``None`` restores local stores."""
+        self.delta_multicast = int(address) if address else None
+        esz = self.delta.element_size()
+        for f in range(len(self.shapes)):
+            self._fields[f].delta_multicast = None if not address else int(address) + esz * self.n_off[f]
 
     def set_base_weight(self, base_weight: torch.Tensor | None) -> None:
         """Fused weight: later forwards store ``W0 + out_scale * value`` (one
@@ -172,21 +187,29 @@ class FieldBatch:
         self._batch.ids = self.ids.data_ptr()
         self._batch.ids_capacity = self.ids.numel()
         self._batch.pair_base = self.pair_base.data_ptr()
-        need = max(self._lib.gf_workspace_bytes(ctypes.byref(self.cfg), ctypes.byref(self._batch), p)
-                   for p in (_lib.GF_PASS_FORWARD, _lib.GF_PASS_BACKWARD))
-        if need == 0:
+        need_f, need_b = (self._lib.gf_workspace_bytes(ctypes.byref(self.cfg), ctypes.byref(self._batch), p)
+                          for p in (_lib.GF_PASS_FORWARD, _lib.GF_PASS_BACKWARD))
+        if need_f == 0 or need_b == 0:
             raise RuntimeError("invalid batch: " + _lib.last_error())
-        if self._ws is None or self._ws.numel() < need:
-            self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        if self._ws is None or self._ws.numel() < need_f:
+            self._ws = torch.zeros(need_f, dtype=torch.uint8, device=self.device)
+        if self._ws_bwd is None or self._ws_bwd.numel() < need_b:
+            self._ws_bwd = torch.zeros(need_b, dtype=torch.uint8, device=self.device)
         self._bound = key
 
     # -- passes --------------------------------------------------------------
     def forward(self, mu, chol_raw, amp, stream=None) -> torch.Tensor:
         """Render every field into ``self.delta``; no host synchronisation."""
+        return self.forward_stages(mu, chol_raw, amp, _lib.GF_STAGE_BIN | _lib.GF_STAGE_RENDER, stream)
+
+    def forward_stages(self, mu, chol_raw, amp, stages: int, stream=None) -> torch.Tensor:
+        """``forward`` in stages (GF_STAGE_BIN, GF_STAGE_RENDER): a backward
+        that needs only this step's binning may start on another stream once
+        the BIN stage is done and overlap the RENDER stage."""
         self._bind(mu, chol_raw, amp)
         st = (stream or torch.cuda.current_stream(self.device)).cuda_stream
-        _lib.check(self._lib.gf_forward(ctypes.byref(self.cfg), ctypes.byref(self._batch), self._ws.data_ptr(),
-                                        self._ws.numel(), st))
+        _lib.check(self._lib.gf_forward_stages(ctypes.byref(self.cfg), ctypes.byref(self._batch), self._ws.data_ptr(),
+                                               self._ws.numel(), int(stages), st))
         return self.delta
 
     def backward(self, grad, mu, chol_raw, amp, stream=None):
@@ -194,17 +217,21 @@ class FieldBatch:
         self._bind(mu, chol_raw, amp)
         self._bind_grad(grad)
         st = (stream or torch.cuda.current_stream(self.device)).cuda_stream
-        _lib.check(self._lib.gf_backward(ctypes.byref(self.cfg), ctypes.byref(self._batch), self._ws.data_ptr(),
-                                         self._ws.numel(), st))
+        _lib.check(self._lib.gf_backward(ctypes.byref(self.cfg), ctypes.byref(self._batch),
+                                         self._ws_bwd.data_ptr(), self._ws_bwd.numel(), st))
         return self.d_mu, self.d_chol_raw, self.d_amp
 
     def device_flags(self, reset: bool = True) -> int:
         """Synchronise and return the GF_FLAG_* bits recorded since the last reset."""
-        flags = ctypes.c_uint32(0)
-        _lib.check(self._lib.gf_workspace_status(self._ws.data_ptr(),
-                                                 torch.cuda.current_stream(self.device).cuda_stream,
-                                                 int(reset), ctypes.byref(flags)))
-        return flags.value
+        out = 0
+        for ws in (self._ws, self._ws_bwd):  # forward flags (capacity) and backward flags (saved state)
+            if ws is None:
+                continue
+            flags = ctypes.c_uint32(0)
+            _lib.check(self._lib.gf_workspace_status(ws.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream,
+                                                     int(reset), ctypes.byref(flags)))
+            out |= flags.value
+        return out
 
     def total_pairs(self) -> int:
         return int(self.pair_base[-1].item())

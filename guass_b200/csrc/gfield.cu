@@ -59,6 +59,7 @@ struct DevField {
   int64_t* ids;
   const void* grad;
   const void* base;   // [out*in] out dtype or nullptr: forward stores base + value
+  unsigned long long mc;  // NVLS multicast address of delta or 0: forward stores go through multimem.st
   float* d_mu;
   float* d_chol;
   float* d_amp;
@@ -180,6 +181,22 @@ __device__ __forceinline__ void add_base8(const __nv_bfloat16* b, float* x) {
     x[2 * k] = __fadd_rn(f.x, x[2 * k]);
     x[2 * k + 1] = __fadd_rn(f.y, x[2 * k + 1]);
   }
+}
+
+// 16-byte output store: to the local delta, or with F.mc to the NVLS
+// multicast address of the same element, so the NVSwitch writes every GPU's
+// copy of the gathered buffer (this one's included) as the tile is produced.
+__device__ __forceinline__ void store16(void* local, unsigned long long mc, size_t byte_off, uint4 v) {
+  if (mc) {
+    asm volatile("multimem.st.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc + byte_off), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+  } else {
+    *reinterpret_cast<uint4*>(static_cast<char*>(local) + byte_off) = v;
+  }
+}
+__device__ __forceinline__ uint4 as_u4(float4 x) {
+  return make_uint4(__float_as_uint(x.x), __float_as_uint(x.y), __float_as_uint(x.z), __float_as_uint(x.w));
 }
 
 // Render-side record of one Gaussian: two float4.
@@ -456,10 +473,11 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
           if (F.vec_ok && q4 + 3 < bw) {
             float4 x = make_float4(s_out[r][q4], s_out[r][q4 + 1], s_out[r][q4 + 2], s_out[r][q4 + 3]);
             if (F.base) x = add_base4(reinterpret_cast<const float*>(F.base) + base + o, x);
-            *reinterpret_cast<float4*>(out + o) = x;
+            store16(F.delta, F.mc, 4 * (base + o), as_u4(x));
           } else {
+            if (F.mc) atomicOr(p.status, GF_FLAG_INTERNAL);  // excluded on the host (vec_ok)
             for (int k = 0; k < 4; ++k)
-              if (q4 + k < bw) {
+              if (!F.mc && q4 + k < bw) {
                 float x = s_out[r][q4 + k];
                 if (F.base) x = __fadd_rn(base_at<GF_F32>(F.base, base + o + k), x);
                 out[o + k] = x;
@@ -483,10 +501,11 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
                 const __nv_bfloat162 h2 = __floats2bfloat162_rn(x[2 * k], x[2 * k + 1]);
                 w[k] = *reinterpret_cast<const uint32_t*>(&h2);
               }
-              *reinterpret_cast<uint4*>(out + o) = make_uint4(w[0], w[1], w[2], w[3]);
+              store16(F.delta, F.mc, 2 * (base + o), make_uint4(w[0], w[1], w[2], w[3]));
             } else {
+              if (F.mc) atomicOr(p.status, GF_FLAG_INTERNAL);  // excluded on the host (vec_ok)
               for (int k = 0; k < 8; ++k)
-                if (q8 + k < bw) {
+                if (!F.mc && q8 + k < bw) {
                   float x = s_out[r][q8 + k];
                   if (F.base) x = __fadd_rn(base_at<GF_BF16>(F.base, base + o + k), x);
                   out[o + k] = __float2bfloat16_rn(x);
@@ -495,6 +514,8 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
           }
         }
       }
+      // multicast stores are published before the caller's group barrier
+      if (F.mc) __threadfence_system();
       __syncthreads();
     }
   }
@@ -658,10 +679,11 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
         if (F.vec_ok && q4 + 3 < tw) {
           float4 x = *reinterpret_cast<const float4*>(&s_out[warp][r][q4]);
           if (F.base) x = add_base4(reinterpret_cast<const float*>(F.base) + base + o, x);
-          *reinterpret_cast<float4*>(out + o) = x;
+          store16(F.delta, F.mc, 4 * (base + o), as_u4(x));
         } else {
+          if (F.mc) atomicOr(p.status, GF_FLAG_INTERNAL);  // excluded on the host (vec_ok)
           for (int j = 0; j < 4; ++j)
-            if (q4 + j < tw) {
+            if (!F.mc && q4 + j < tw) {
               float x = s_out[warp][r][q4 + j];
               if (F.base) x = __fadd_rn(base_at<GF_F32>(F.base, base + o + j), x);
               out[o + j] = x;
@@ -687,12 +709,13 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
           }
           const __nv_bfloat162 h0 = __floats2bfloat162_rn(x0.x, x0.y), h1 = __floats2bfloat162_rn(x0.z, x0.w);
           const __nv_bfloat162 h2 = __floats2bfloat162_rn(x1.x, x1.y), h3 = __floats2bfloat162_rn(x1.z, x1.w);
-          *reinterpret_cast<uint4*>(out + o) =
-              make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
-                         *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3));
+          store16(F.delta, F.mc, 2 * (base + o),
+                  make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
+                             *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3)));
         } else {
+          if (F.mc) atomicOr(p.status, GF_FLAG_INTERNAL);  // excluded on the host (vec_ok)
           for (int j = 0; j < 8; ++j)
-            if (q8 + j < tw) {
+            if (!F.mc && q8 + j < tw) {
               float x = s_out[warp][r][q8 + j];
               if (F.base) x = __fadd_rn(base_at<GF_BF16>(F.base, base + o + j), x);
               out[o + j] = __float2bfloat16_rn(x);
@@ -701,6 +724,8 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
       }
     }
   }
+  // multicast stores are published before the caller's group barrier
+  if (F.mc) __threadfence_system();
 }
 
 // ---------------------------------------------------------------------------
@@ -1214,6 +1239,14 @@ gf_status validate(const gf_config* cfg, const gf_batch* batch, gf_pass pass, bo
       return fail(GF_ERR_INVALID_ARG, "field %d: gaussian_ids must be non-null", i);
     if (!batch->ids && f.ids_capacity < 0) return fail(GF_ERR_INVALID_ARG, "field %d: ids_capacity must be >= 0", i);
     if (pass == GF_PASS_FORWARD && !f.delta) return fail(GF_ERR_INVALID_ARG, "field %d: delta must be non-null", i);
+    if (pass == GF_PASS_FORWARD && f.delta_multicast) {
+      const int64_t vec = cfg->out_dtype == GF_F32 ? 4 : 8;  // elements per 16-byte store
+      if (((reinterpret_cast<uintptr_t>(f.delta) | reinterpret_cast<uintptr_t>(f.delta_multicast)) & 15u) ||
+          f.in_features % vec || cfg->tile_in % vec)
+        return fail(GF_ERR_UNSUPPORTED,
+                    "field %d: delta_multicast needs 16-byte aligned delta rows (aligned delta and multicast "
+                    "address, in_features and tile_in multiples of %lld)", i, (long long)vec);
+    }
     if (pass == GF_PASS_BACKWARD) {
       if (!f.grad_delta) return fail(GF_ERR_INVALID_ARG, "field %d: grad_delta must be non-null", i);
       if (f.num_gaussians > 0 && (!f.d_mu || !f.d_chol_raw || !f.d_amp))
@@ -1286,6 +1319,7 @@ void fill_params(Params<NF>& P, const gf_config* cfg, const gf_batch* batch, con
     d.delta = s.delta; d.tile_ptr = s.tile_ptr; d.ids = s.gaussian_ids; d.grad = s.grad_delta;
     d.d_mu = s.d_mu; d.d_chol = s.d_chol_raw; d.d_amp = s.d_amp;
     d.base = s.base_weight;
+    d.mc = reinterpret_cast<unsigned long long>(s.delta_multicast);
     d.ids_cap = s.ids_capacity;
     d.part_base = part_base;
     if (!batch->ids) part_base += s.ids_capacity;
@@ -1315,7 +1349,8 @@ void fill_params(Params<NF>& P, const gf_config* cfg, const gf_batch* batch, con
   } while (0)
 
 template <int NF>
-gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout& L, char* ws, cudaStream_t st) {
+gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout& L, char* ws, cudaStream_t st,
+                      unsigned stages = GF_STAGE_BIN | GF_STAGE_RENDER) {
   // The descriptor block is large; keep one per thread instead of on the stack.
   thread_local Params<NF>* tp = nullptr;
   if (!tp) tp = new Params<NF>();
@@ -1332,10 +1367,13 @@ gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout&
     cudaFuncSetAttribute(bin_kernel<NF>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBinSmemCapInts * 4);
     attr_set = true;
   }
-  trace_mark(st);
-  bin_kernel<NF><<<p.n, kBinThreads, smem, st>>>(p, kBinSmemCapInts);
-  GF_LAUNCH_CHECK("bin_kernel");
-  trace_mark(st);
+  if (stages & GF_STAGE_BIN) {
+    trace_mark(st);
+    bin_kernel<NF><<<p.n, kBinThreads, smem, st>>>(p, kBinSmemCapInts);
+    GF_LAUNCH_CHECK("bin_kernel");
+    trace_mark(st);
+  }
+  if (!(stages & GF_STAGE_RENDER)) return GF_OK;
   const bool norm = p.cfg.normalize, clamp = p.cfg.has_clamp;
   const int grid = (int)L.total_tiles;
 #define GF_FWD(N, C, O)                                                                         \
@@ -1429,7 +1467,7 @@ size_t gf_workspace_bytes(const gf_config* cfg, const gf_batch* batch, gf_pass p
 }
 
 static gf_status gf_dispatch(const gf_config* cfg, const gf_batch* batch, void* workspace, size_t workspace_bytes,
-                             gf_stream stream, gf_pass pass) {
+                             gf_stream stream, gf_pass pass, unsigned stages = GF_STAGE_BIN | GF_STAGE_RENDER) {
   gf_status s = gf::validate(cfg, batch, pass);
   if (s != GF_OK) return s;
   const gf::Layout L = gf::layout(cfg, batch, pass);
@@ -1442,9 +1480,9 @@ static gf_status gf_dispatch(const gf_config* cfg, const gf_batch* batch, void* 
   char* ws = static_cast<char*>(workspace);
   const int n = batch->num_fields;
   if (pass == GF_PASS_FORWARD) {
-    if (n == 1) return gf::run_forward<1>(cfg, batch, L, ws, st);
-    if (n <= 16) return gf::run_forward<16>(cfg, batch, L, ws, st);
-    return gf::run_forward<GF_MAX_FIELDS>(cfg, batch, L, ws, st);
+    if (n == 1) return gf::run_forward<1>(cfg, batch, L, ws, st, stages);
+    if (n <= 16) return gf::run_forward<16>(cfg, batch, L, ws, st, stages);
+    return gf::run_forward<GF_MAX_FIELDS>(cfg, batch, L, ws, st, stages);
   }
   if (n == 1) return gf::run_backward<1>(cfg, batch, L, ws, st);
   if (n <= 16) return gf::run_backward<16>(cfg, batch, L, ws, st);
@@ -1454,6 +1492,13 @@ static gf_status gf_dispatch(const gf_config* cfg, const gf_batch* batch, void* 
 gf_status gf_forward(const gf_config* cfg, const gf_batch* batch, void* workspace, size_t workspace_bytes,
                      gf_stream stream) {
   return gf_dispatch(cfg, batch, workspace, workspace_bytes, stream, GF_PASS_FORWARD);
+}
+
+gf_status gf_forward_stages(const gf_config* cfg, const gf_batch* batch, void* workspace, size_t workspace_bytes,
+                            unsigned stages, gf_stream stream) {
+  if (stages == 0 || (stages & ~(GF_STAGE_BIN | GF_STAGE_RENDER)))
+    return gf::fail(GF_ERR_INVALID_ARG, "stages must be GF_STAGE_BIN, GF_STAGE_RENDER or both");
+  return gf_dispatch(cfg, batch, workspace, workspace_bytes, stream, GF_PASS_FORWARD, stages);
 }
 
 gf_status gf_backward(const gf_config* cfg, const gf_batch* batch, void* workspace, size_t workspace_bytes,

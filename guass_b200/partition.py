@@ -117,10 +117,18 @@ class PartitionedRenderer:
     gathered delta) runs.  A symmetric-memory barrier ends the exchange.
     Elsewhere it falls back to one in-place NCCL all-gather on the side
     stream, overlapped with the backward.
+
+    ``fused=True`` (multicast only) removes the separate publish: the render
+    kernel itself stores every output row through the multicast address
+    (``gf_field.delta_multicast``), so the transfer leaves tile by tile while
+    the render computes.  The step then bins, starts the backward on the side
+    stream as soon as the binning is done (it overlaps the render, which waits
+    on NVLink ingress more than on arithmetic), renders with multicast stores,
+    and ends with the symmetric-memory barrier.
     """
 
     def __init__(self, shapes, costs, rank: int, world: int, group=None, device=None, groups: int = 4,
-                 use_multicast: bool | None = None, publish_blocks: int = 64, **batch_kw):
+                 use_multicast: bool | None = None, publish_blocks: int = 64, fused: bool = False, **batch_kw):
         from guass_b200 import _lib
         from guass_b200.batched import FieldBatch
 
@@ -149,14 +157,16 @@ class PartitionedRenderer:
                     self.gathered = buf.view(world, self.layout.slot)
             except (RuntimeError, AttributeError, ImportError):
                 self.symm = None
-            if use_multicast and self.symm is None:
+            if (use_multicast or fused) and self.symm is None:
                 raise RuntimeError("NVLink multicast is not available for this group")
         if self.symm is None:
             self.gathered = torch.zeros(world, self.layout.slot, dtype=out_dtype, device=dev)
-        self.exchange = "nvls-multicast" if self.symm is not None else ("nccl-all-gather" if world > 1 else "none")
+        self.fused = bool(fused) and self.symm is not None
+        self.exchange = ("nvls-multicast-fused-render" if self.fused else "nvls-multicast") if self.symm is not None \
+            else ("nccl-all-gather" if world > 1 else "none")
         # field groups: contiguous runs of this rank's fields (slot order), balanced by cost
         own_costs = [max(1, costs[i]) for i in self.own]
-        ng = max(1, min(groups if self.symm is not None else 1, len(self.own)))
+        ng = max(1, min(groups if self.symm is not None and not self.fused else 1, len(self.own)))
         total, bounds, acc, g = sum(own_costs), [0], 0, 1
         for j, c in enumerate(own_costs):
             acc += c
@@ -170,8 +180,11 @@ class PartitionedRenderer:
             fs = self.own[g0:g1]
             n0 = self.n_off[-1]
             n1 = n0 + sum(numels[i] for i in fs)
+            mc = None
+            if self.fused:
+                mc = self.mc_ptr + (rank * self.layout.slot + n0) * self.gathered.element_size()
             self.batches.append(FieldBatch([shapes[i] for i in fs], out_dtype=out_dtype, device=dev,
-                                           delta_out=self.gathered[rank, n0:n1], **batch_kw))
+                                           delta_out=self.gathered[rank, n0:n1], delta_multicast=mc, **batch_kw))
             self.n_off.append(n1)
             self.k_off.append(self.k_off[-1] + sum(int(shapes[i][2]) for i in fs))
         self.side = torch.cuda.Stream(device=dev) if world > 1 else None
@@ -205,9 +218,32 @@ class PartitionedRenderer:
         self._lib.check(self._lib.lib().gf_multicast_store(src, self.mc_ptr + base * elt, nbytes,
                                                            self.publish_blocks, self.side.cuda_stream))
 
+    def _step_fused(self, mu, chol_raw, amp, grad):
+        from guass_b200 import _lib
+
+        main = torch.cuda.current_stream(self.device)
+        b = self.batches[0]
+        b.forward_stages(mu, chol_raw, amp, _lib.GF_STAGE_BIN, main)
+        self.side.wait_stream(main)
+        with torch.cuda.stream(self.side):
+            out = b.backward(grad, mu, chol_raw, amp, stream=self.side)
+        ev = None
+        if self.gather_events is not None:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record(main)
+        b.forward_stages(mu, chol_raw, amp, _lib.GF_STAGE_RENDER, main)  # multicast stores
+        self.symm.barrier()
+        if ev is not None:
+            ev[1].record(main)
+            self.gather_events.append(ev)
+        main.wait_stream(self.side)
+        return [out]
+
     def step(self, mu, chol_raw, amp, grad):
         """Forward + exchange + backward for this rank's packed parameters
         (fields in ``own`` order); returns the packed gradients."""
+        if self.fused:
+            return self._step_fused(mu, chol_raw, amp, grad)
         main = torch.cuda.current_stream(self.device)
         ev = None
         if self.world > 1 and self.gather_events is not None:

@@ -106,6 +106,17 @@ typedef struct gf_field {
    * (in place).  The backward is unchanged: grad_delta is dL/d(value),
    * which for W_eff = W0 + out_scale * value is out_scale * dL/dW_eff. */
   const void* base_weight;
+  /* Optional NVLink multicast (NVLS) address of `delta` (NULL = plain
+   * stores).  The forward then writes every output row through multimem
+   * stores to this address, so the switch updates the copy of `delta` on
+   * every GPU bound to the multicast object while the tile is produced --
+   * the render and the all-gather of the result are one kernel.  It needs
+   * 16-byte aligned rows (delta and this address 16-byte aligned, in_features
+   * and tile_in multiples of 16/sizeof(out_dtype)); other fields are
+   * rejected with GF_ERR_UNSUPPORTED.  The kernel ends with a system-scope
+   * fence; the caller synchronises the group (a barrier) before any GPU
+   * reads the result. */
+  void* delta_multicast;
 } gf_field;
 
 /* A batch of fields rendered by one set of launches.
@@ -126,6 +137,10 @@ typedef enum gf_pass { GF_PASS_FORWARD = 0, GF_PASS_BACKWARD = 1 } gf_pass;
 
 /* ABI version compiled into the library (GF_ABI_VERSION). */
 int gf_abi_version(void);
+
+/* Stages of gf_forward, for gf_forward_stages. */
+#define GF_STAGE_BIN 1u    /* per-field preprocess + binning: tile_ptr, ids, pair_base */
+#define GF_STAGE_RENDER 2u /* the delta render, from the binning and workspace of the BIN stage */
 
 /* Message for the last non-OK status returned on this thread. */
 const char* gf_last_error(void);
@@ -164,6 +179,15 @@ gf_status gf_workspace_status(void* workspace, gf_stream stream, int reset, uint
  * turns tracing off.  gf_trace_count() returns how many have been recorded. */
 gf_status gf_trace_events(void* const* events, int n);
 int gf_trace_count(void);
+
+/* gf_forward in stages: `stages` is GF_STAGE_BIN, GF_STAGE_RENDER or both
+ * (== gf_forward).  A RENDER stage must follow a BIN stage of the same batch,
+ * parameters and workspace, in stream order.  Work that needs only the
+ * binning -- gf_backward on another stream with its own workspace -- may
+ * start once the BIN stage is complete, so that it overlaps the render.
+ * Trace events: BIN records 2 (start, bin), RENDER 1 (render). */
+gf_status gf_forward_stages(const gf_config* cfg, const gf_batch* batch, void* workspace, size_t workspace_bytes,
+                            unsigned stages, gf_stream stream);
 
 /* Multi-GPU publish (no reference counterpart; GUASS has no layer
  * partitioning).  Copies `bytes` from the local device buffer `src` to

@@ -54,7 +54,7 @@ int main(void) {
   printf("gf_batch %zu\n", sizeof(gf_batch));
   printf("gf_stats_layer %zu\n", sizeof(gf_stats_layer));
   F(gf_config, clamp_quad) F(gf_config, out_scale) F(gf_config, grad_dtype)
-  F(gf_field, row_coords) F(gf_field, ids_capacity) F(gf_field, d_amp) F(gf_field, base_weight)
+  F(gf_field, row_coords) F(gf_field, ids_capacity) F(gf_field, d_amp) F(gf_field, base_weight) F(gf_field, delta_multicast)
   F(gf_batch, fields) F(gf_batch, ids_capacity) F(gf_batch, pair_base)
   F(gf_stats_layer, d_mu_raw) F(gf_stats_layer, amp) F(gf_stats_layer, stats)
   return 0;
@@ -170,3 +170,27 @@ def test_grad_stats_argument_errors():
     assert L.gf_grad_stats_accumulate(1, layers, None) == _lib.GF_ERR_INVALID_ARG
     layers[0].num_gaussians = 0  # nothing to do: no launch
     assert L.gf_grad_stats_accumulate(2, layers, None) == _lib.GF_OK
+
+
+def test_forward_stages_and_multicast_arguments():
+    L = _lib.lib()
+    fake = 1 << 20  # never dereferenced: validation fails first
+    kw = dict(row_coords=fake, col_coords=fake, mu=fake, chol_raw=fake, amp=fake, delta=fake, tile_ptr=fake,
+              gaussian_ids=fake, ids_capacity=100)
+    b, keep = _batch(**kw)
+    for bad in (0, 4, 7):
+        st = L.gf_forward_stages(ctypes.byref(_cfg()), ctypes.byref(b), None, 0, bad, None)
+        assert st == _lib.GF_ERR_INVALID_ARG and "stages" in _lib.last_error()
+    # multicast stores need 16-byte rows: bf16 needs in_features % 8 == 0, an aligned address
+    b, keep = _batch(**dict(kw, in_features=70, delta_multicast=1 << 21))
+    st = L.gf_forward(ctypes.byref(_cfg(out_dtype=_lib.GF_BF16)), ctypes.byref(b), None, 0, None)
+    assert st == _lib.GF_ERR_UNSUPPORTED and "delta_multicast" in _lib.last_error()
+    b, keep = _batch(**dict(kw, delta_multicast=(1 << 21) + 8))
+    st = L.gf_forward(ctypes.byref(_cfg(out_dtype=_lib.GF_BF16)), ctypes.byref(b), None, 0, None)
+    assert st == _lib.GF_ERR_UNSUPPORTED
+    b, keep = _batch(**dict(kw, delta_multicast=1 << 21))
+    st = L.gf_forward(ctypes.byref(_cfg(out_dtype=_lib.GF_BF16, tile_in=12)), ctypes.byref(b), None, 0, None)
+    assert st == _lib.GF_ERR_UNSUPPORTED
+    # an aligned request passes validation and fails on the missing workspace instead
+    st = L.gf_forward(ctypes.byref(_cfg(out_dtype=_lib.GF_BF16)), ctypes.byref(b), None, 0, None)
+    assert st == _lib.GF_ERR_INVALID_ARG and "workspace" in _lib.last_error()

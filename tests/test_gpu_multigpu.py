@@ -3,8 +3,9 @@
 Each rank renders its share of 16 fields with PartitionedRenderer; after one
 step every rank must hold every field's bf16 delta, bit-identical to a
 single-GPU render of the same field, and its own fields' gradients must equal
-the single-GPU gradients.  Run for both exchanges: NVLink multicast (when the
-GPUs have it) and the NCCL all-gather.
+the single-GPU gradients.  Run for every exchange: NVLink multicast publish
+(when the GPUs have it), the NCCL all-gather, and the render kernel storing
+through the multicast address ("fused", skipped without NVLink multicast).
 """
 from __future__ import annotations
 
@@ -41,7 +42,15 @@ def _worker(rank, world, port, use_mc, q):
         fields = synthetic.cfg3()[:16]
         shapes = [(f.out_features, f.in_features, f.k) for f in fields]
         costs = [f.numel for f in fields]
-        r = PartitionedRenderer(shapes, costs, rank, world, groups=3, use_multicast=use_mc)
+        fused = use_mc == "fused"
+        try:
+            r = PartitionedRenderer(shapes, costs, rank, world, groups=3, use_multicast=None if fused else use_mc,
+                                    fused=fused)
+        except RuntimeError as exc:
+            if "multicast is not available" not in str(exc):
+                raise
+            q.put((rank, False, str(exc), "unavailable"))
+            return
         own = [fields[i] for i in r.own]
         mu, chol, amp, grad = pack_fields(own, device=dev)
         r.ensure_capacity(mu, chol, amp)
@@ -68,7 +77,7 @@ def _worker(rank, world, port, use_mc, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("use_mc", [None, False])
+@pytest.mark.parametrize("use_mc", [None, False, "fused"])
 def test_partitioned_render_two_gpus(use_mc):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -81,6 +90,8 @@ def test_partitioned_render_two_gpus(use_mc):
     for p in procs:
         p.join(timeout=300)
     res = [q.get(timeout=30) for _ in procs]
+    if use_mc == "fused" and any("multicast is not available" in m for _, _, m, _ in res):
+        pytest.skip("no NVLink multicast between these GPUs")
     assert all(p.exitcode == 0 for p in procs)
     for rank, ok, msg, exchange in res:
         assert ok, f"rank {rank} ({exchange}): {msg}"
