@@ -81,11 +81,13 @@ class GaussianProjection(nn.Module):
             self.weight = nn.Parameter(torch.empty(out_features, in_features, dtype=dtype), requires_grad=False)
             self.mu_raw, self.chol_raw, self.amp = (nn.Parameter(torch.empty(k, c)) for c in (2, 3, 1))
             return
-        g = torch.Generator().manual_seed(10_000 + seed)
-        w = torch.randn(out_features, in_features, generator=g, device="cpu") / math.sqrt(in_features)
+        # seeded on the host (CPU generators), whatever the default device; model.to() moves them
+        with torch.device("cpu"):
+            g = torch.Generator().manual_seed(10_000 + seed)
+            w = torch.randn(out_features, in_features, generator=g) / math.sqrt(in_features)
+            f = synthetic.make_field(out_features, in_features, k, seed=seed, log_scale_mean=math.log(0.03),
+                                     log_scale_std=0.5)
         self.weight = nn.Parameter(w.to(dtype), requires_grad=False)
-        f = synthetic.make_field(out_features, in_features, k, seed=seed, log_scale_mean=math.log(0.03),
-                                 log_scale_std=0.5)
         self.mu_raw = nn.Parameter(torch.atanh(f.mu.clamp(-0.999, 0.999)))
         self.chol_raw = nn.Parameter(f.chol_raw.clone())
         self.amp = nn.Parameter(f.amp.clone())
