@@ -107,3 +107,33 @@ def test_peer_death_surfaces_as_an_error():
         if p.is_alive():
             p.kill()
     assert rank == 0 and outcome != "completed"
+
+
+def _fused_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from guass_b200.partition import PartitionedRenderer
+        try:
+            PartitionedRenderer([(64, 64, 4), (32, 32, 4)], [10, 5], rank, world, device=torch.device("cpu"),
+                                fused=True)
+            q.put((rank, "constructed"))
+        except RuntimeError as exc:
+            q.put((rank, str(exc)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_fused_exchange_without_multicast_fails_loudly():
+    """The multicast-fused render has no silent fallback: without NVLink
+    multicast (here: CPU ranks) the renderer refuses to build."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fused_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert all("multicast is not available" in m for m in res.values()), res
