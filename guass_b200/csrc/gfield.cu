@@ -607,9 +607,11 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
 #pragma unroll
   for (int i = 0; i < R / 2; ++i)
     CR[i] = pk2(__shfl_sync(0xffffffffu, myr, 2 * i), __shfl_sync(0xffffffffu, myr, 2 * i + 1));
-  float v[R];
+  // row pairs (2i, 2i+1) accumulate in packed registers: fma.rn.f32x2 rounds
+  // each half exactly like the scalar fmaf of forward.cu:361
+  f2 V[R / 2];
 #pragma unroll
-  for (int i = 0; i < R; ++i) v[i] = 0.0f;
+  for (int i = 0; i < R / 2; ++i) V[i] = pk2(0.0f, 0.0f);
 
   int64_t found = 0;
   for (int k0 = 0; k0 < F.K && found < count; k0 += 32) {
@@ -634,7 +636,7 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
       const float a01 = __fmul_rn(h.y, dy);
       const float a11 = __fmul_rn(h.z, dy);
       const f2 H00 = pk2(h.x, h.x), H01 = pk2(h.y, h.y), A01 = pk2(a01, a01), A11 = pk2(a11, a11);
-      const f2 DY = pk2(dy, dy), MUR = pk2(a.x, a.x);
+      const f2 DY = pk2(dy, dy), MUR = pk2(a.x, a.x), AMP = pk2(a.z, a.z);
 #pragma unroll
       for (int i = 0; i < R / 2; ++i) {
         const f2 DX = sub2(CR[i], MUR);
@@ -654,8 +656,7 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
           e0 = __fmul_rn(e0, a.w);
           e1 = __fmul_rn(e1, a.w);
         }
-        v[2 * i] = __fmaf_rn(a.z, e0, v[2 * i]);
-        v[2 * i + 1] = __fmaf_rn(a.z, e1, v[2 * i + 1]);
+        V[i] = fma2(AMP, pk2(e0, e1), V[i]);
       }
     }
   }
@@ -664,7 +665,12 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
   // Stage the warp's R x 32 block and store it with 128-bit stores.
   const float sc = p.cfg.out_scale;
 #pragma unroll
-  for (int i = 0; i < R; ++i) s_out[warp][i][lane] = (sc != 1.0f) ? __fmul_rn(v[i], sc) : v[i];
+  for (int i = 0; i < R / 2; ++i) {
+    float v0, v1;
+    up2(V[i], v0, v1);
+    s_out[warp][2 * i][lane] = (sc != 1.0f) ? __fmul_rn(v0, sc) : v0;
+    s_out[warp][2 * i + 1][lane] = (sc != 1.0f) ? __fmul_rn(v1, sc) : v1;
+  }
   __syncwarp();
   const int bh = min(R, th - rw0);
   if (bh <= 0) return;
@@ -960,7 +966,7 @@ __device__ __forceinline__ PairSums bwd32_pair_rows(const float* s_rows, const f
     }
     const float2 gg = *reinterpret_cast<const float2*>(&s_gcol[2 * k]);
     const f2 GB = mul2(pk2(gg.x, gg.y), pk2(e0, e1));
-    S.T0 = add2(S.T0, GB);
+    if (TRACK_CLAMP) S.T0 = add2(S.T0, GB);  // without clamped elements T0 == U0 (same terms, same order)
     f2 GBA = GB;
     if (TRACK_CLAMP) {
       float b0, b1;
@@ -971,6 +977,7 @@ __device__ __forceinline__ PairSums bwd32_pair_rows(const float* s_rows, const f
     S.U1 = fma2(GBA, DX, S.U1);
     S.U2 = fma2(mul2(GBA, DX), DX, S.U2);
   }
+  if (!TRACK_CLAMP) S.T0 = S.U0;
   return S;
 }
 
