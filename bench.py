@@ -445,6 +445,24 @@ def reference_arm(a, rank, world):
 
 
 # ---------------------------------------------------------------------------
+SFU_EX2_PER_CLK = 16  # per SM
+
+
+def step_roofline(evals_total, bytes_step, ms, sm_count, f_mhz, hbm_peak, world):
+    """Whole-step bound: t_bound = max(bytes / HBM, 2E / SFU, FP32 ops / FP32)
+    over the job's GPUs, E the exact (element, Gaussian) evaluations (one
+    exp each in the forward and the backward), FP32 ops = E x (9 + 25)."""
+    clk = f_mhz * 1e6
+    terms = {"hbm_ms": bytes_step / (hbm_peak * 1e9 * world) * 1e3,
+             "sfu_ms": 2 * evals_total / (sm_count * SFU_EX2_PER_CLK * clk * world) * 1e3,
+             "fp32_ms": evals_total * sum(OPS_PER_EVAL.values()) / (sm_count * SM_FP32_LANES * clk * world) * 1e3}
+    bound = max(terms, key=terms.get)
+    return {"t_bound_ms": terms[bound], "binding": bound[:-3], "t_measured_ms": ms, "frac": terms[bound] / ms,
+            "terms": terms, "clock_mhz": f_mhz,
+            "definition": "t_bound / t_measured; peaks: HBM = MEASURED_PEAKS.json hbm_gbs, SFU = SMs x 16 ex2/clk, "
+                          "FP32 = SMs x 128 lanes, at the sampled SM clock"}
+
+
 def load_traffic(kernel: str):
     p = ROOT / "profiles" / f"{kernel}_unet_traffic.json"
     if p.exists():
@@ -687,6 +705,8 @@ def main():
                                    f"per launch / CUDA-event launch time; peak = {sm_count} SMs x "
                                    f"{SM_FP32_LANES} FP32 lanes x {f_mhz:.0f} MHz (sampled SM clock; "
                                    "MEASURED_PEAKS.json has no FP32 figure)"},
+        "roofline_step": step_roofline(evals_total=w.total_evals, bytes_step=bytes_step, ms=ms, sm_count=sm_count,
+                                       f_mhz=f_mhz, hbm_peak=hbm_peak, world=world),
         "roofline_hbm": {"achieved": bytes_step / (ms / 1e3) / 1e9, "peak": hbm_peak, "unit": "GB/s",
                          "frac": bytes_step / (ms / 1e3) / 1e9 / hbm_peak, "peak_source": "MEASURED_PEAKS.json hbm_gbs"},
         "clocks": clocks,
