@@ -18,6 +18,9 @@ ROOT = PKG.parent
 SOURCES = [PKG / "csrc" / "gfield.cu"]
 HEADERS = [ROOT / "include" / "gfield.h"]
 LIB = PKG / "libgfield.so"
+# debug build: every shape-derived global access bounds-checked (GF_FLAG_BOUNDS);
+# load it instead of the release library with GUASS_B200_LIB=<path>
+LIB_CHECK = PKG / "libgfield_check.so"
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -33,24 +36,32 @@ def nvcc() -> str:
     return str(cand) if cand.exists() else "nvcc"
 
 
-def needs_build() -> bool:
-    if not LIB.exists():
+def needs_build(lib: Path = LIB) -> bool:
+    if not lib.exists():
         return True
-    t = LIB.stat().st_mtime
+    t = lib.stat().st_mtime
     return any(p.stat().st_mtime > t for p in SOURCES + HEADERS)
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    if not force and not needs_build():
-        return LIB
-    tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc(), *NVCC_FLAGS, f"-I{ROOT / 'include'}", *map(str, SOURCES), "-o", str(tmp), "-lcudart"]
+def build(force: bool = False, verbose: bool = False, check: bool = False) -> Path:
+    """Build the release library (or, with ``check``, the bounds-checked one)."""
+    lib = LIB_CHECK if check else LIB
+    if not force and not needs_build(lib):
+        return lib
+    tmp = lib.with_suffix(".so.tmp")
+    cmd = [nvcc(), *NVCC_FLAGS, *(["-DGF_CHECK"] if check else []), f"-I{ROOT / 'include'}", *map(str, SOURCES),
+           "-o", str(tmp), "-lcudart"]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True)
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib)
+    return lib
+
+
+def build_all(force: bool = False, verbose: bool = False) -> list[Path]:
+    return [build(force, verbose), build(force, verbose, check=True)]
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose=True))
+    for lib in build_all(force="--force" in sys.argv, verbose=True):
+        print(lib)

@@ -39,6 +39,7 @@ GF_STAGE_RENDER = 2
 GF_FLAG_CAPACITY = 0x1
 GF_FLAG_STATE = 0x2
 GF_FLAG_INTERNAL = 0x4
+GF_FLAG_BOUNDS = 0x8
 
 # Every symbol include/gfield.h declares.
 EXPORTED = ("gf_abi_version", "gf_last_error", "gf_num_tiles", "gf_workspace_bytes", "gf_forward",

@@ -18,6 +18,7 @@
 
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <cstdarg>
 #include <cstdint>
@@ -96,6 +97,20 @@ struct Params {
 };
 // __grid_constant__ parameters are limited to 32764 bytes per launch.
 static_assert(sizeof(Params<GF_MAX_FIELDS>) <= 32764, "descriptor block exceeds the kernel-parameter limit");
+
+// Bounds checks of the debug build (-DGF_CHECK, libgfield_check.so): every
+// shape-derived global access is tested against its extent; a failure sets
+// GF_FLAG_BOUNDS in the workspace and the access is skipped (never a trap).
+// In the release build the check is the constant true and compiles away.
+#ifdef GF_CHECK
+__device__ __forceinline__ bool gf_bounds_ok(bool ok, uint32_t* status) {
+  if (!ok) atomicOr(status, GF_FLAG_BOUNDS);
+  return ok;
+}
+#define GF_IN_BOUNDS(cond) gf_bounds_ok((cond), p.status)
+#else
+#define GF_IN_BOUNDS(cond) true
+#endif
 
 // ---------------------------------------------------------------------------
 // Geometry (forward.cu:134-209), bit-exact.
@@ -406,7 +421,7 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
       for (int k0 = 0; k0 < F.K && found < count; k0 += kChunk) {
         const int g = k0 + tid;
         bool hit = false;
-        if (g < F.K) {
+        if (g < F.K && GF_IN_BOUNDS(F.g_base + g < p.total_g)) {
           const int4 b = box[g];
           hit = (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
         }
@@ -470,14 +485,15 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
         const int r = tid >> 3, q4 = (tid & 7) * 4;
         if (r < bh) {
           const size_t o = (size_t)r * F.in_f + q4;
-          if (F.vec_ok && q4 + 3 < bw) {
+          const size_t nel = (size_t)F.out_f * F.in_f;
+          if (F.vec_ok && q4 + 3 < bw && GF_IN_BOUNDS(base + o + 3 < nel)) {
             float4 x = make_float4(s_out[r][q4], s_out[r][q4 + 1], s_out[r][q4 + 2], s_out[r][q4 + 3]);
             if (F.base) x = add_base4(reinterpret_cast<const float*>(F.base) + base + o, x);
             store16(F.delta, F.mc, 4 * (base + o), as_u4(x));
           } else {
             if (F.mc) atomicOr(p.status, GF_FLAG_INTERNAL);  // excluded on the host (vec_ok)
             for (int k = 0; k < 4; ++k)
-              if (!F.mc && q4 + k < bw) {
+              if (!F.mc && q4 + k < bw && GF_IN_BOUNDS(base + o + k < nel)) {
                 float x = s_out[r][q4 + k];
                 if (F.base) x = __fadd_rn(base_at<GF_F32>(F.base, base + o + k), x);
                 out[o + k] = x;
@@ -490,7 +506,8 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
           const int r = tid >> 2, q8 = (tid & 3) * 8;
           if (r < bh) {
             const size_t o = (size_t)r * F.in_f + q8;
-            if (F.vec_ok && q8 + 7 < bw) {
+            const size_t nel = (size_t)F.out_f * F.in_f;
+            if (F.vec_ok && q8 + 7 < bw && GF_IN_BOUNDS(base + o + 7 < nel)) {
               float x[8];
 #pragma unroll
               for (int k = 0; k < 8; ++k) x[k] = s_out[r][q8 + k];
@@ -505,7 +522,7 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
             } else {
               if (F.mc) atomicOr(p.status, GF_FLAG_INTERNAL);  // excluded on the host (vec_ok)
               for (int k = 0; k < 8; ++k)
-                if (!F.mc && q8 + k < bw) {
+                if (!F.mc && q8 + k < bw && GF_IN_BOUNDS(base + o + k < nel)) {
                   float x = s_out[r][q8 + k];
                   if (F.base) x = __fadd_rn(base_at<GF_BF16>(F.base, base + o + k), x);
                   out[o + k] = __float2bfloat16_rn(x);
@@ -617,7 +634,7 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
   for (int k0 = 0; k0 < F.K && found < count; k0 += 32) {
     const int g = k0 + lane;
     bool hit = false;
-    if (g < F.K) {
+    if (g < F.K && GF_IN_BOUNDS(F.g_base + g < p.total_g)) {
       const int4 b = box[g];
       hit = (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
     }
@@ -682,14 +699,15 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
       const int r = k * 4 + (lane >> 3), q4 = (lane & 7) * 4;
       if (r < bh) {
         const size_t o = (size_t)r * F.in_f + q4;
-        if (F.vec_ok && q4 + 3 < tw) {
+        const size_t nel = (size_t)F.out_f * F.in_f;
+        if (F.vec_ok && q4 + 3 < tw && GF_IN_BOUNDS(base + o + 3 < nel)) {
           float4 x = *reinterpret_cast<const float4*>(&s_out[warp][r][q4]);
           if (F.base) x = add_base4(reinterpret_cast<const float*>(F.base) + base + o, x);
           store16(F.delta, F.mc, 4 * (base + o), as_u4(x));
         } else {
           if (F.mc) atomicOr(p.status, GF_FLAG_INTERNAL);  // excluded on the host (vec_ok)
           for (int j = 0; j < 4; ++j)
-            if (!F.mc && q4 + j < tw) {
+            if (!F.mc && q4 + j < tw && GF_IN_BOUNDS(base + o + j < nel)) {
               float x = s_out[warp][r][q4 + j];
               if (F.base) x = __fadd_rn(base_at<GF_F32>(F.base, base + o + j), x);
               out[o + j] = x;
@@ -704,7 +722,8 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
       const int r = k * 8 + (lane >> 2), q8 = (lane & 3) * 8;
       if (r < bh) {
         const size_t o = (size_t)r * F.in_f + q8;
-        if (F.vec_ok && q8 + 7 < tw) {
+        const size_t nel = (size_t)F.out_f * F.in_f;
+        if (F.vec_ok && q8 + 7 < tw && GF_IN_BOUNDS(base + o + 7 < nel)) {
           float4 x0 = *reinterpret_cast<const float4*>(&s_out[warp][r][q8]);
           float4 x1 = *reinterpret_cast<const float4*>(&s_out[warp][r][q8 + 4]);
           if (F.base) {
@@ -721,7 +740,7 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
         } else {
           if (F.mc) atomicOr(p.status, GF_FLAG_INTERNAL);  // excluded on the host (vec_ok)
           for (int j = 0; j < 8; ++j)
-            if (!F.mc && q8 + j < tw) {
+            if (!F.mc && q8 + j < tw && GF_IN_BOUNDS(base + o + j < nel)) {
               float x = s_out[warp][r][q8 + j];
               if (F.base) x = __fadd_rn(base_at<GF_BF16>(F.base, base + o + j), x);
               out[o + j] = __float2bfloat16_rn(x);
@@ -833,7 +852,9 @@ render_bwd_kernel(const __grid_constant__ Params<NF> p) {
   float* s_row = s_g + TO * TI;
   for (int e = tid; e < TO * TI; e += blockDim.x) {
     const int r = e / TI, c = e - r * TI;
-    s_g[e] = (r < th && c < tw) ? load_grad<GT>(F.grad, (size_t)(row0 + r) * F.in_f + col0 + c) : 0.0f;
+    s_g[e] = (r < th && c < tw && GF_IN_BOUNDS((size_t)(row0 + r) * F.in_f + col0 + c < (size_t)F.out_f * F.in_f))
+                 ? load_grad<GT>(F.grad, (size_t)(row0 + r) * F.in_f + col0 + c)
+                 : 0.0f;
   }
   for (int r = tid; r < TO; r += blockDim.x) s_row[r] = (r < th) ? F.row[row0 + r] : 0.0f;
   __syncthreads();
@@ -1014,7 +1035,10 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
   if (threadIdx.x < 32) s_rows[threadIdx.x] = (threadIdx.x < th) ? F.row[row0 + threadIdx.x] : 0.0f;
   for (int e = threadIdx.x; e < 1024; e += blockDim.x) {
     const int r = e >> 5, c = e & 31;
-    s_gt[c * 34 + r] = (r < th && c < tw) ? load_grad<GT>(F.grad, (size_t)(row0 + r) * F.in_f + col0 + c) : 0.0f;
+    s_gt[c * 34 + r] =
+        (r < th && c < tw && GF_IN_BOUNDS((size_t)(row0 + r) * F.in_f + col0 + c < (size_t)F.out_f * F.in_f))
+            ? load_grad<GT>(F.grad, (size_t)(row0 + r) * F.in_f + col0 + c)
+            : 0.0f;
   }
   __syncthreads();
   if (warp >= count) return;
@@ -1184,6 +1208,16 @@ struct Trace {
   int used = 0;
 };
 thread_local Trace g_trace;
+
+// NVTX range over the host-side enqueue of one stage ("gfield.<stage>"), so a
+// timeline profiler shows each entry point and kernel launch by name.  A
+// no-op unless a tool is attached.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 inline void trace_mark(cudaStream_t st) {
   if (g_trace.used < g_trace.n) {
@@ -1375,12 +1409,14 @@ gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout&
     attr_set = true;
   }
   if (stages & GF_STAGE_BIN) {
+    NvtxRange r("gfield.bin");
     trace_mark(st);
     bin_kernel<NF><<<p.n, kBinThreads, smem, st>>>(p, kBinSmemCapInts);
     GF_LAUNCH_CHECK("bin_kernel");
     trace_mark(st);
   }
   if (!(stages & GF_STAGE_RENDER)) return GF_OK;
+  NvtxRange r("gfield.render_fwd");
   const bool norm = p.cfg.normalize, clamp = p.cfg.has_clamp;
   const int grid = (int)L.total_tiles;
 #define GF_FWD(N, C, O)                                                                         \
@@ -1423,13 +1459,17 @@ gf_status run_backward(const gf_config* cfg, const gf_batch* batch, const Layout
   if (!tp) tp = new Params<NF>();
   Params<NF>& p = *tp;
   fill_params(p, cfg, batch, L, ws);
-  trace_mark(st);
-  bwd_prep_kernel<NF><<<p.n, kBinThreads, 0, st>>>(p);
-  GF_LAUNCH_CHECK("bwd_prep_kernel");
-  trace_mark(st);
+  {
+    NvtxRange r("gfield.bwd_prep");
+    trace_mark(st);
+    bwd_prep_kernel<NF><<<p.n, kBinThreads, 0, st>>>(p);
+    GF_LAUNCH_CHECK("bwd_prep_kernel");
+    trace_mark(st);
+  }
   const bool norm = p.cfg.normalize, clamp = p.cfg.has_clamp;
   const int grid = (int)L.total_tiles;
   const size_t smem = sizeof(float) * ((size_t)cfg->tile_out * cfg->tile_in + cfg->tile_out);
+  NvtxRange r("gfield.render_bwd+finalize");
 #define GF_BWD(N, C, G) launch_bwd_render<NF, N, C, G>(p, grid, smem, st)
   if (cfg->grad_dtype == GF_F32) {
     if (norm) { if (clamp) GF_BWD(true, true, GF_F32); else GF_BWD(true, false, GF_F32); }
@@ -1486,6 +1526,7 @@ static gf_status gf_dispatch(const gf_config* cfg, const gf_batch* batch, void* 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(workspace);
   const int n = batch->num_fields;
+  gf::NvtxRange r(pass == GF_PASS_FORWARD ? "gfield.forward" : "gfield.backward");
   if (pass == GF_PASS_FORWARD) {
     if (n == 1) return gf::run_forward<1>(cfg, batch, L, ws, st, stages);
     if (n <= 16) return gf::run_forward<16>(cfg, batch, L, ws, st, stages);
@@ -1564,6 +1605,7 @@ extern "C" gf_status gf_multicast_store(const void* src, void* mc_dst, size_t by
   if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(mc_dst) | bytes) & 15u)
     return gf::fail(GF_ERR_INVALID_ARG, "gf_multicast_store: src, mc_dst and bytes must be multiples of 16");
   if (max_blocks <= 0) return gf::fail(GF_ERR_INVALID_ARG, "gf_multicast_store: max_blocks must be positive");
+  gf::NvtxRange r("gfield.multicast_store");
   const size_t n16 = bytes / 16;
   const int threads = 512;
   const size_t need = (n16 + threads - 1) / threads;
@@ -1613,6 +1655,7 @@ extern "C" gf_status gf_grad_stats_accumulate(int32_t num_layers, const gf_stats
   if (num_layers < 0 || num_layers > GF_MAX_FIELDS || !layers)
     return gf::fail(GF_ERR_INVALID_ARG, "gf_grad_stats_accumulate: num_layers must be in 0..%d with a layer array",
                     GF_MAX_FIELDS);
+  gf::NvtxRange r("gfield.grad_stats");
   thread_local gf::StatsParams* tp = nullptr;
   if (!tp) tp = new gf::StatsParams();
   gf::StatsParams& p = *tp;

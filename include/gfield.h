@@ -62,6 +62,8 @@ typedef enum gf_dtype { GF_F32 = 0, GF_BF16 = 1 } gf_dtype;
 #define GF_FLAG_CAPACITY 0x1u /* pairs exceeded ids capacity; ids truncated */
 #define GF_FLAG_STATE 0x2u    /* backward: tile_ptr/ids do not match mu/chol_raw */
 #define GF_FLAG_INTERNAL 0x4u /* forward: per-tile list disagreed with tile_ptr */
+#define GF_FLAG_BOUNDS 0x8u   /* debug build (libgfield_check.so) only: an index fell outside its
+                                 buffer; the access was skipped */
 
 /* Render options; mirrors ForwardConfig (gaussian_peft/cuda_field/csrc/field.h:11-18)
  * plus the output/gradient storage types. */

@@ -21,7 +21,7 @@ def pytest_configure(config):
     from guass_b200 import _build
     import oracle
 
-    _build.build()
+    _build.build_all()
     oracle.build()
 
 

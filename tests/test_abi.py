@@ -194,3 +194,14 @@ def test_forward_stages_and_multicast_arguments():
     # an aligned request passes validation and fails on the missing workspace instead
     st = L.gf_forward(ctypes.byref(_cfg(out_dtype=_lib.GF_BF16)), ctypes.byref(b), None, 0, None)
     assert st == _lib.GF_ERR_INVALID_ARG and "workspace" in _lib.last_error()
+
+
+def test_checked_build_exports_the_same_abi():
+    """libgfield_check.so (-DGF_CHECK) is a drop-in replacement of the release library."""
+    from guass_b200 import _build
+
+    lib = ctypes.CDLL(str(_build.LIB_CHECK))
+    for name in _lib.EXPORTED:
+        assert hasattr(lib, name), name
+    lib.gf_abi_version.restype = ctypes.c_int
+    assert lib.gf_abi_version() == _lib.GF_ABI_VERSION
