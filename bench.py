@@ -492,7 +492,8 @@ def train_arm(a, rank: int, world: int, local: int) -> None:
         model = sd15.SD15UNet(cfg, dtype=torch.bfloat16)
     model.cuda()
     mods = model.adapters()
-    bank = BatchedAdapters(mods, out_dtype=torch.bfloat16, fused_weight=(a.adapter_apply == "fused"))
+    bank = BatchedAdapters(mods, out_dtype=torch.bfloat16, fused_weight=(a.adapter_apply == "fused"),
+                           track_metadata=False)  # no per-step diagnostic read-back in the timed loop
     bank.install()
     tr = sd15.DataParallelTrainer(model, bank, world=world)
     inp = sd15.synthetic_inputs(cfg, a.batch, seed=1000 + rank, device="cuda")

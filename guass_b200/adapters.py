@@ -93,7 +93,8 @@ class BatchedAdapters:
     :meth:`refresh_base` after changing a base weight.
     """
 
-    def __init__(self, modules: dict, batch_factory=None, out_dtype=torch.bfloat16, fused_weight: bool = False):
+    def __init__(self, modules: dict, batch_factory=None, out_dtype=torch.bfloat16, fused_weight: bool = False,
+                 track_metadata: bool = True):
         self.names = list(modules)
         self.modules = [modules[n] for n in self.names]
         if not self.modules:
@@ -109,6 +110,7 @@ class BatchedAdapters:
                   normalize=cfg.normalize_gaussian, clamp_quad=80.0,  # gaussian_linear.py:189
                   out_dtype=out_dtype, grad_dtype=out_dtype)
         self.fused = bool(fused_weight)
+        self.track_metadata = bool(track_metadata)
         self.w0 = None
         if self.fused:
             scales = {float(m.adapter_config.adapter_scale) for m in self.modules}
@@ -165,7 +167,8 @@ class BatchedAdapters:
     def rebuilt(self) -> "BatchedAdapters":
         """A new binding for the modules' current K (keeps install state)."""
         fresh = BatchedAdapters(dict(zip(self.names, self.modules)), batch_factory=self._factory,
-                                out_dtype=self._out_dtype, fused_weight=self.fused)
+                                out_dtype=self._out_dtype, fused_weight=self.fused,
+                                track_metadata=self.track_metadata)
         if self._orig:
             self.uninstall()
             fresh.install()
@@ -220,6 +223,8 @@ class BatchedAdapters:
             self.ensure_capacity()
         mu, chol, amp = self._packed_params()
         packed = BatchedFieldFunction.apply(self.batch, mu, chol, amp)
+        if self.track_metadata:
+            self._publish_metadata(packed.detach())
         out = []
         for f, m in enumerate(self.modules):
             d = packed[self.n_off[f]:self.n_off[f + 1]].view(m.out_features, m.in_features)
@@ -227,6 +232,25 @@ class BatchedAdapters:
             out.append(d * scale if scale != 1.0 and not self.fused else d)
         self._current = out
         return out
+
+    def _publish_metadata(self, packed):
+        """Each module's ``last_forward_metadata`` with the keys GaussianLinear
+        writes (gaussian_linear.py:196-219) and GUASS's diagnostics read
+        (utils/logging.py:17-62): execution_mode, accumulate_backend and
+        delta_w_norm (of the unscaled delta, as the layer computes it).  The
+        norms of all layers come from one fused launch and one host read (the
+        layer itself reads one per layer); the fused mode renders W0 + delta
+        and reports no norm."""
+        meta = {"execution_mode": "cuda_field_train", "accumulate_backend": "gfield_batched"}
+        norms = [None] * len(self.modules)
+        if not self.fused:
+            views = [packed[self.n_off[f]:self.n_off[f + 1]] for f in range(len(self.modules))]
+            norms = torch.stack(torch._foreach_norm(views, 2, dtype=torch.float32)).tolist()
+        for m, n in zip(self.modules, norms):
+            md = dict(meta)
+            if n is not None:
+                md["delta_w_norm"] = float(n)
+            m.last_forward_metadata = md
 
     def _slot(self, f):
         if self._current is None:

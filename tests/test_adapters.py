@@ -317,3 +317,18 @@ def test_pair_capacity_bound_or_measured(monkeypatch):
     bank.render()
     bank.render()
     assert bank.batch.capacity_checks == 1  # measured once, on the first render
+
+
+def test_render_publishes_layer_metadata():
+    mods = _modules()
+    bank = BatchedAdapters(mods, batch_factory=OracleBatch)
+    deltas = bank.render()
+    for m, d in zip(mods.values(), deltas):
+        md = m.last_forward_metadata
+        assert md["execution_mode"] == "cuda_field_train" and md["accumulate_backend"] == "gfield_batched"
+        # the norm of the unscaled delta, like GaussianLinear.compute_delta_weight
+        want = float((d / m.adapter_config.adapter_scale).detach().float().norm())
+        assert abs(md["delta_w_norm"] - want) <= 1e-5 * want
+    quiet = _modules()
+    BatchedAdapters(quiet, batch_factory=OracleBatch, track_metadata=False).render()
+    assert not hasattr(quiet["a"], "last_forward_metadata")
