@@ -77,3 +77,30 @@ def test_oracle_vs_reference_torch_random_config(seed):
         if b.size == 0:
             continue
         assert np.abs(a - b).max() <= 1e-4 * max(np.abs(b).max(), 1e-30), n
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 3, 32, 32), (3, 200, 4, 64, 64), (130, 1, 6, 8, 8), (5, 7, 0, 32, 32)])
+def test_oracle_vs_reference_torch_degenerate_shapes(shape):
+    """1x1 fields, single rows and columns, tiles larger than the field, and
+    K = 0 (forward only: the reference's autograd has nothing to differentiate)."""
+    out_f, in_f, k, to, ti = shape
+    f = make_field(out_f, in_f, k, seed=1, log_scale_mean=math.log(0.2))
+    kw = dict(tile_out=to, tile_in=ti, sigma_multiplier=3.0, normalize=False, clamp_quad=80.0)
+    d, tp, ids = oracle.forward(f.row_coords, f.col_coords, f.mu, f.chol_raw, f.amp, **kw)
+    if k == 0:
+        from gaussian_peft.kernels.covariance import activate_cholesky
+        from gaussian_peft.kernels.gaussian_field import gaussian_field
+
+        rd, meta = gaussian_field(torch.zeros(1, 2), f.mu, activate_cholesky(f.chol_raw, eps=1e-5), f.amp,
+                                  clamp_quad=80.0, execution_mode="tiled_reference_pytorch", row_coords=f.row_coords,
+                                  col_coords=f.col_coords, tile_out=to, tile_in=ti, return_metadata=True)
+        assert not d.any() and not rd.numpy().any()
+        np.testing.assert_array_equal(tp, meta["tile_ptr"].numpy())
+        assert ids.size == 0
+        return
+    rd, rtp, rids, rg = _ref(f, to, ti, 3.0, False, 80.0)
+    np.testing.assert_array_equal(tp, rtp)
+    assert np.abs(d - rd).max() <= 1e-5 * max(np.abs(rd).max(), 1e-30)
+    g = oracle.backward(f.grad, f.row_coords, f.col_coords, f.mu, f.chol_raw, f.amp, tp, ids, **kw)
+    for a, b, n in zip(g, rg, ("d_mu", "d_chol_raw", "d_amp")):
+        assert np.abs(a - b).max() <= 1e-4 * max(np.abs(b).max(), 1e-30), n
