@@ -48,6 +48,8 @@ def test_normalize_and_clamp_variants(normalize, clamp):
     ((100, 200), (64, 64)),  # tiles larger than one 32x32 sub-block
     ((90, 77), (7, 13)),     # odd tile sizes
     ((64, 300), (8, 96)),    # wide tiles, 3 column sub-blocks
+    ((1, 1), (32, 32)),      # one element
+    ((3, 20), (64, 64)),     # one tile larger than the whole field
 ])
 def test_tile_shapes(shape, tiles):
     f = random_field(shape[0], shape[1], 30, seed=5, mean_scale=0.1)
