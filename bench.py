@@ -71,6 +71,9 @@ def parse_args():
     ap.add_argument("--adapter-apply", choices=["fused", "reference"], default="fused",
                     help="cfg4: one GEMM on W0+delta, or the reference layer's base GEMM + row-chunked delta GEMMs")
     ap.add_argument("--batch", type=int, default=4, help="cfg4: samples per GPU")
+    ap.add_argument("--bwd-exp", choices=["expf", "ex2"], default="expf",
+                    help="backward basis: CUDA expf (default) or the base-2 hardware approximation "
+                         "(GF_CFG_BWD_EXP2; the forward's delta is bit-exact either way)")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
     return a
@@ -161,7 +164,7 @@ def sum_over_ranks(x: float, world: int) -> float:
 class UNetWorkload:
     """Fields of the whole UNet, partitioned; this rank's batch and buffers."""
 
-    def __init__(self, rank: int, world: int, exchange: str = "auto", groups: int = 4):
+    def __init__(self, rank: int, world: int, exchange: str = "auto", groups: int = 4, bwd_exp2: bool = False):
         from guass_b200 import synthetic
         from guass_b200.batched import FieldBatch, pack_fields
         from guass_b200.partition import PartitionedRenderer, field_costs
@@ -184,7 +187,7 @@ class UNetWorkload:
         del full, mu, chol, amp
         use_mc = {"auto": False, "multicast": True, "fused": True, "nccl": False}[exchange]
         self.renderer = PartitionedRenderer(shapes, self.costs, rank, world, groups=groups, use_multicast=use_mc,
-                                            fused=(exchange == "fused"))
+                                            fused=(exchange == "fused"), bwd_exp2=bwd_exp2)
         self.parts, self.own = self.renderer.parts, self.renderer.own
         self.layout, self.gathered = self.renderer.layout, self.renderer.gathered
         own_fields = [self.fields[i] for i in self.own]
@@ -621,7 +624,7 @@ def main():
         reference_arm(a, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))
         return
     rank, world, local = setup_dist()
-    w = UNetWorkload(rank, world, a.exchange, a.groups)
+    w = UNetWorkload(rank, world, a.exchange, a.groups, bwd_exp2=(a.bwd_exp == "ex2"))
     sampler = ClockSampler() if local == 0 else None
     if sampler:
         sampler.start()
@@ -693,6 +696,7 @@ def main():
         "config": {"workload": "cfg3 whole-UNet batched render, 128 projection fields, K=256",
                    "elements": w.total_elements, "pairs": w.total_pairs, "evals": w.total_evals,
                    "delta_dtype": "bf16", "grad_dtype": "f32", "tile": "32x32", "sigma_multiplier": 3.0,
+                   "backward_basis": "ex2.approx" if a.bwd_exp == "ex2" else "expf",
                    "clamp_quad": 80.0, "partition": f"LPT by render cost over {world} rank(s)",
                    "parallelism": f"layer-partition x{world} + {w.renderer.exchange} of bf16 delta "
                                   f"({len(w.renderer.batches)} field groups)" if world > 1 else "single GPU",

@@ -34,6 +34,7 @@ GF_BF16 = 1
 GF_PASS_FORWARD = 0
 GF_PASS_BACKWARD = 1
 
+GF_CFG_BWD_EXP2 = 0x1
 GF_STAGE_BIN = 1
 GF_STAGE_RENDER = 2
 GF_FLAG_CAPACITY = 0x1
@@ -59,6 +60,7 @@ class GfConfig(ctypes.Structure):
         ("out_scale", ctypes.c_float),
         ("out_dtype", ctypes.c_int32),
         ("grad_dtype", ctypes.c_int32),
+        ("flags", ctypes.c_uint32),
     ]
 
 

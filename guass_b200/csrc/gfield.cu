@@ -46,6 +46,7 @@ struct Cfg {
   float nclamp;     // -0.5f * (float)clamp_quad (exact scaling)
   float out_scale;
   int32_t has_clamp, normalize;
+  uint32_t flags;   // gf_config.flags
 };
 
 // One field as the kernels see it (kernel-parameter space, read via LDC).
@@ -957,7 +958,21 @@ struct PairSums {
 };
 
 // Sum over the 32 rows of one lane's column for one pair.
-template <bool NORM, bool TRACK_CLAMP>
+// Backward basis with GF_CFG_BWD_EXP2: exp(q) = 2^(q * log2 e), one
+// multiply and the hardware base-2 approximation (ex2.approx.ftz).  The
+// rounding of the product costs a relative error of about |q| * 6e-8 in the
+// basis, i.e. at most ~2e-8 of the largest term once weighted by e^q (q <= 0);
+// ex2.approx adds a few 1e-7.  Every gradient term keeps its relative
+// accuracy to ~3e-7, inside the backward's tolerance.  The forward always
+// uses CUDA's expf, which the bit parity of delta requires.
+constexpr float kLog2e = 1.44269504088896340736f;
+__device__ __forceinline__ float exp_via_ex2(float q) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(__fmul_rn(q, kLog2e)));
+  return r;
+}
+
+template <bool NORM, bool TRACK_CLAMP, bool EX2>
 __device__ __forceinline__ PairSums bwd32_pair_rows(const float* s_rows, const float* s_gcol, f2 H00, f2 H01,
                                                    f2 A01, f2 A11, f2 DY, f2 MUR, float nclamp, float nf) {
   const f2 zero2 = pk2(0.0f, 0.0f);
@@ -980,7 +995,14 @@ __device__ __forceinline__ PairSums bwd32_pair_rows(const float* s_rows, const f
       q0 = fmaxf(q0, nclamp);
       q1 = fmaxf(q1, nclamp);
     }
-    float e0 = expf(q0), e1 = expf(q1);
+    float e0, e1;
+    if (EX2) {
+      e0 = exp_via_ex2(q0);
+      e1 = exp_via_ex2(q1);
+    } else {
+      e0 = expf(q0);
+      e1 = expf(q1);
+    }
     if (NORM) {
       e0 = __fmul_rn(e0, nf);
       e1 = __fmul_rn(e1, nf);
@@ -1010,7 +1032,7 @@ __device__ __forceinline__ float corner_bound(float dx, float dy, float h00, flo
   return q - 1e-5f * s;
 }
 
-template <int NF, bool NORM, bool CLAMP, int GT>
+template <int NF, bool NORM, bool CLAMP, int GT, bool EX2>
 __global__ void __launch_bounds__(32 * kBwd32Warps)
 render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
   __shared__ __align__(16) float s_rows[32];
@@ -1085,8 +1107,8 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
                              fminf(corner_bound(dx1, dy0, h.x, h.y, h.z), corner_bound(dx1, dy1, h.x, h.y, h.z)));
       track = !(lo > nclamp);
     }
-    PairSums S = track ? bwd32_pair_rows<NORM, true>(s_rows, s_gcol, H00, H01, A01, A11, DY, MUR, nclamp, a.w)
-                       : bwd32_pair_rows<NORM, false>(s_rows, s_gcol, H00, H01, A01, A11, DY, MUR, nclamp, a.w);
+    PairSums S = track ? bwd32_pair_rows<NORM, true, EX2>(s_rows, s_gcol, H00, H01, A01, A11, DY, MUR, nclamp, a.w)
+                       : bwd32_pair_rows<NORM, false, EX2>(s_rows, s_gcol, H00, H01, A01, A11, DY, MUR, nclamp, a.w);
     float t0a, t0b, u0a, u0b, u1a, u1b, u2a, u2b;
     up2(S.T0, t0a, t0b);
     up2(S.U0, u0a, u0b);
@@ -1335,6 +1357,7 @@ void fill_params(Params<NF>& P, const gf_config* cfg, const gf_batch* batch, con
   P.cfg.out_scale = cfg->out_scale;
   P.cfg.has_clamp = cfg->has_clamp_quad != 0;
   P.cfg.normalize = cfg->normalize != 0;
+  P.cfg.flags = cfg->flags;
   P.n = batch->num_fields;
   P.total_tiles = (int32_t)L.total_tiles;
   P.total_g = (int32_t)L.total_g;
@@ -1441,7 +1464,8 @@ gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout&
 template <int NF, bool N, bool C, int G>
 void launch_bwd_render(const Params<NF>& p, int grid, size_t smem, cudaStream_t st) {
   if (p.cfg.tile_out == 32 && p.cfg.tile_in == 32) {
-    render_bwd32_kernel<NF, N, C, G><<<grid, 32 * kBwd32Warps, 0, st>>>(p);
+    if (p.cfg.flags & GF_CFG_BWD_EXP2) render_bwd32_kernel<NF, N, C, G, true><<<grid, 32 * kBwd32Warps, 0, st>>>(p);
+    else render_bwd32_kernel<NF, N, C, G, false><<<grid, 32 * kBwd32Warps, 0, st>>>(p);
     return;
   }
   static bool attr_set = false;

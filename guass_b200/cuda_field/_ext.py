@@ -87,12 +87,12 @@ def _validate_forward_inputs(row_coords, col_coords, mu, chol_raw, amp) -> None:
 
 
 def make_config(tile_out, tile_in, sigma_multiplier, normalize, clamp_quad, *, out_dtype=_lib.GF_F32,
-                grad_dtype=_lib.GF_F32, out_scale=1.0) -> _lib.GfConfig:
+                grad_dtype=_lib.GF_F32, out_scale=1.0, flags=0) -> _lib.GfConfig:
     return _lib.GfConfig(
         tile_out=int(tile_out), tile_in=int(tile_in), sigma_multiplier=float(sigma_multiplier),
         normalize=int(bool(normalize)), has_clamp_quad=int(clamp_quad is not None),
         clamp_quad=float(clamp_quad) if clamp_quad is not None else 0.0,
-        out_scale=float(out_scale), out_dtype=int(out_dtype), grad_dtype=int(grad_dtype))
+        out_scale=float(out_scale), out_dtype=int(out_dtype), grad_dtype=int(grad_dtype), flags=int(flags))
 
 
 class WorkspacePool:

@@ -78,7 +78,14 @@ typedef struct gf_config {
                          the backward takes dL/d(value), i.e. the caller scales */
   int32_t out_dtype;  /* gf_dtype of delta */
   int32_t grad_dtype; /* gf_dtype of grad_delta */
+  uint32_t flags;     /* GF_CFG_* options, 0 = the reference's arithmetic */
 } gf_config;
+
+/* gf_config.flags: the 32x32-tile backward evaluates its basis as
+ * exp(q) = 2^(q*log2 e) with the hardware base-2 approximation instead of
+ * expf (a few 1e-7 relative per term; the backward is tolerance-bound, the
+ * forward's delta stays bit-exact either way). */
+#define GF_CFG_BWD_EXP2 0x1u
 
 /* One field (layer).  Forward reads the inputs and writes delta, tile_ptr and
  * (in per-field id mode) gaussian_ids; backward reads grad_delta, tile_ptr and

@@ -53,7 +53,7 @@ int main(void) {
   printf("gf_field %zu\n", sizeof(gf_field));
   printf("gf_batch %zu\n", sizeof(gf_batch));
   printf("gf_stats_layer %zu\n", sizeof(gf_stats_layer));
-  F(gf_config, clamp_quad) F(gf_config, out_scale) F(gf_config, grad_dtype)
+  F(gf_config, clamp_quad) F(gf_config, out_scale) F(gf_config, grad_dtype) F(gf_config, flags)
   F(gf_field, row_coords) F(gf_field, ids_capacity) F(gf_field, d_amp) F(gf_field, base_weight) F(gf_field, delta_multicast)
   F(gf_batch, fields) F(gf_batch, ids_capacity) F(gf_batch, pair_base)
   F(gf_stats_layer, d_mu_raw) F(gf_stats_layer, amp) F(gf_stats_layer, stats)
