@@ -245,7 +245,11 @@ class BatchedAdapters:
         norms = [None] * len(self.modules)
         if not self.fused:
             views = [packed[self.n_off[f]:self.n_off[f + 1]] for f in range(len(self.modules))]
-            norms = torch.stack(torch._foreach_norm(views, 2, dtype=torch.float32)).tolist()
+            try:
+                parts = torch._foreach_norm(views, 2, dtype=torch.float32)  # one fused launch
+            except (RuntimeError, TypeError):
+                parts = [torch.linalg.vector_norm(v, dtype=torch.float32) for v in views]
+            norms = torch.stack(list(parts)).tolist()
         for m, n in zip(self.modules, norms):
             md = dict(meta)
             if n is not None:
