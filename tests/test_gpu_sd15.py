@@ -26,7 +26,10 @@ def _grads(model):
     return [p.grad.clone() for m in model.adapters().values() for p in (m.mu_raw, m.chol_raw, m.amp)]
 
 
-def test_fused_and_reference_composition_agree_fp32():
+def test_fused_and_reference_composition_agree_fp32(monkeypatch):
+    # plain fp32 everywhere (cuDNN would otherwise run the convolutions in TF32)
+    monkeypatch.setattr(torch.backends.cudnn, "allow_tf32", False)
+    monkeypatch.setattr(torch.backends.cuda.matmul, "allow_tf32", False)
     out = []
     for fused in (False, True):
         model, bank, tr = _setup(fused, torch.float32)
