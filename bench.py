@@ -68,8 +68,10 @@ def parse_args():
     ap.add_argument("--workload", choices=["cfg3", "cfg4"], default="cfg3",
                     help="cfg3: whole-UNet batched render (default, the headline); cfg4: data-parallel "
                          "SD1.5-UNet adapter training step")
-    ap.add_argument("--adapter-apply", choices=["fused", "reference"], default="fused",
-                    help="cfg4: one GEMM on W0+delta, or the reference layer's base GEMM + row-chunked delta GEMMs")
+    ap.add_argument("--adapter-apply", choices=["fused", "reference", "dropin"], default="fused",
+                    help="cfg4: one batched render and one GEMM on W0+delta (fused); one batched render and the "
+                         "reference layer's base GEMM + row-chunked delta GEMMs (reference); every layer rendering "
+                         "itself through the drop-in runtime, the reference's call pattern (dropin)")
     ap.add_argument("--batch", type=int, default=4, help="cfg4: samples per GPU")
     ap.add_argument("--bwd-exp", choices=["expf", "ex2"], default="expf",
                     help="backward basis: CUDA expf (default) or the base-2 hardware approximation "
@@ -495,8 +497,11 @@ def train_arm(a, rank: int, world: int, local: int) -> None:
         model = sd15.SD15UNet(cfg, dtype=torch.bfloat16)
     model.cuda()
     mods = model.adapters()
-    bank = BatchedAdapters(mods, out_dtype=torch.bfloat16, fused_weight=(a.adapter_apply == "fused"),
-                           track_metadata=False)  # no per-step diagnostic read-back in the timed loop
+    if a.adapter_apply == "dropin":
+        bank = sd15.PerLayerRender(mods)
+    else:
+        bank = BatchedAdapters(mods, out_dtype=torch.bfloat16, fused_weight=(a.adapter_apply == "fused"),
+                               track_metadata=False)  # no per-step diagnostic read-back in the timed loop
     bank.install()
     tr = sd15.DataParallelTrainer(model, bank, world=world)
     inp = sd15.synthetic_inputs(cfg, a.batch, seed=1000 + rank, device="cuda")
@@ -506,19 +511,28 @@ def train_arm(a, rank: int, world: int, local: int) -> None:
     for _ in range(a.warmup):
         tr.step(inp)
     torch.cuda.synchronize()
-    assert bank.batch.device_flags() == 0
     nf = len(shapes)
-    tps = [bank.batch.tile_ptr_view(i).cpu() for i in range(nf)]
+    # exact evaluation count from one binning pass of the current parameters
+    probe = bank if a.adapter_apply != "dropin" else BatchedAdapters(mods, track_metadata=False)
+    with torch.no_grad():
+        probe.render()
+    assert probe.batch.device_flags() == 0
+    tps = [probe.batch.tile_ptr_view(i).cpu() for i in range(nf)]
     evals = sum(field_costs(tps, shapes))
     elements = sum(o * i for o, i in shapes)
+    del probe
+    calls = nf if a.adapter_apply == "dropin" else 1  # library forward/backward calls per step
 
     sampler = ClockSampler() if local == 0 else None
     if sampler:
         sampler.start()
         time.sleep(0.3)
         sampler.mark("t0")
-    # per step: 3 trace events in the render forward, 4 in its backward (gfield.h, gf_trace_events)
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(7 * a.steps)]
+    # per step and call: 3 trace events in the render forward, 4 in its backward (gfield.h,
+    # gf_trace_events); all forward calls of a step come before its backward calls
+    expected = 7 * calls * a.steps
+    # headroom: a drop-in forward that outgrows its id buffer renders again (3 more events)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(expected + (3 * calls * a.steps if calls > 1 else 0))]
     for e in evs:
         e.record()
     torch.cuda.synchronize()
@@ -537,15 +551,25 @@ def train_arm(a, rank: int, world: int, local: int) -> None:
     _lib.check(L.gf_trace_events(None, 0))
     if sampler:
         sampler.mark("t1")
-    assert recorded == len(evs), (recorded, len(evs))
     ms = max_over_ranks(start.elapsed_time(end) / a.steps, world)
     per = {"render_fwd": [], "render_bwd": [], "render_total": []}
-    for st in range(a.steps):
-        e = evs[7 * st: 7 * (st + 1)]
-        per["render_fwd"].append(e[1].elapsed_time(e[2]))
-        per["render_bwd"].append(e[4].elapsed_time(e[5]))
-        per["render_total"].append(e[0].elapsed_time(e[2]) + e[3].elapsed_time(e[6]))
-    kern = {k: max_over_ranks(sum(v) / len(v), world) for k, v in per.items()}
+    if recorded != expected:  # a re-render shifted the events: no per-kernel attribution
+        assert calls > 1, (recorded, expected)
+        per = {}
+    for st in range(a.steps if per else 0):
+        e = evs[7 * calls * st: 7 * calls * (st + 1)]
+        fw = [e[3 * c: 3 * c + 3] for c in range(calls)]
+        bw = [e[3 * calls + 4 * c: 3 * calls + 4 * c + 4] for c in range(calls)]
+        per["render_fwd"].append(sum(f[1].elapsed_time(f[2]) for f in fw))
+        per["render_bwd"].append(sum(b[1].elapsed_time(b[2]) for b in bw))
+        per["render_total"].append(sum(f[0].elapsed_time(f[2]) for f in fw) + sum(b[0].elapsed_time(b[3]) for b in bw))
+    ok = torch.tensor([1.0 if per else 0.0], device="cuda")
+    if world > 1:
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if ok.item() > 0:
+        kern = {k: max_over_ranks(sum(v) / len(v), world) for k, v in per.items()}
+    else:
+        kern = {"unavailable": "a drop-in forward re-rendered for a larger id buffer inside the timed loop"}
     clocks = sampler.stop() if sampler else None
     assert torch.isfinite(loss).item()
 
@@ -575,8 +599,14 @@ def train_arm(a, rank: int, world: int, local: int) -> None:
     if rank == 0:
         sm_count = torch.cuda.get_device_properties(0).multi_processor_count
         f_mhz = (clocks or {}).get("sm_mhz") or 1965.0
-        achieved = evals * OPS_PER_EVAL["render_bwd"] / (kern["render_bwd"] / 1e3) / 1e12
         peak = sm_count * SM_FP32_LANES * f_mhz * 1e6 / 1e12
+        roofline = None
+        if "render_bwd" in kern:
+            achieved = evals * OPS_PER_EVAL["render_bwd"] / (kern["render_bwd"] / 1e3) / 1e12
+            roofline = {"kernel": "render_bwd", "bound": "fp32", "achieved": achieved, "peak": peak,
+                        "unit": "Tops/s", "frac": achieved / peak, "traffic": None,
+                        "definition": "as the cfg3 line: 25 FMA-pipe ops per evaluation / CUDA-event launch time"
+                                      + (" (summed over the per-layer launches)" if calls > 1 else "")}
         samples = a.batch * world
         line = {
             "metric": TRAIN_METRIC, "value": samples / (ms / 1e3), "unit": "samples/s", "n_gpus": world,
@@ -590,17 +620,15 @@ def train_arm(a, rank: int, world: int, local: int) -> None:
                        "parallelism": f"dp{world}: flat NCCL all-reduce of Gaussian-parameter gradients"
                        if world > 1 else "single GPU", "optimizer": "AdamW on mu_raw/chol_raw/amp",
                        "l2": "no flush: the UNet step streams GBs of activations and weights"},
-            "kernels_ms": kern, "render_share": kern["render_total"] / ms,
-            "roofline": {"kernel": "render_bwd", "bound": "fp32", "achieved": achieved, "peak": peak,
-                         "unit": "Tops/s", "frac": achieved / peak, "traffic": None,
-                         "definition": "as the cfg3 line: 25 FMA-pipe ops per evaluation / CUDA-event launch time"},
+            "kernels_ms": kern, "render_share": kern["render_total"] / ms if "render_total" in kern else None,
+            "roofline": roofline,
             "clocks": clocks,
             "e2e": {"value": samples / (e2e_ms / 1e3), "unit": "samples/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": int(h2d * world), "d2h_bytes_per_step": 4 * world,
                     "path": "DataParallelTrainer.step with latents/text/t/noise H2D from pinned memory "
                             "and the loss read back, every step"},
             "cpu_baseline": None,
-            "gpu_launches": 5 * a.steps * world,
+            "gpu_launches": 5 * calls * a.steps * world,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -292,6 +292,44 @@ def diffusion_loss(model: SD15UNet, inp: StepInputs, alphas_cumprod) -> torch.Te
     return F.mse_loss(pred.float(), inp.noise.float())
 
 
+class PerLayerRender:
+    """The reference's call pattern: every GaussianProjection renders its own
+    delta inside its forward through the drop-in runtime
+    (``guass_b200.cuda_field.gaussian_field_train``, i.e. what
+    GaussianLinear.compute_delta_weight does in ``cuda_field_train`` mode,
+    gaussian_linear.py:178-197): one render and one backward per layer.
+    ``render()`` is a no-op so that it can stand in for
+    :class:`~guass_b200.adapters.BatchedAdapters` in :class:`DataParallelTrainer`."""
+
+    def __init__(self, modules: dict):
+        self.modules = list(modules.values())
+        self._orig = {}
+
+    def install(self):
+        from guass_b200.cuda_field import gaussian_field_train
+
+        for m in self.modules:
+            if id(m) in self._orig:
+                continue
+            self._orig[id(m)] = m.compute_delta_weight
+            dev = m.mu_raw.device
+            rows = torch.linspace(-1.0, 1.0, m.out_features, device=dev)
+            cols = torch.linspace(-1.0, 1.0, m.in_features, device=dev)
+
+            def cdw(m=m, rows=rows, cols=cols):
+                c = m.adapter_config
+                delta = gaussian_field_train(row_coords=rows, col_coords=cols, mu=torch.tanh(m.mu_raw),
+                                             chol_raw=m.chol_raw, amp=m.amp, tile_out=c.tile_out, tile_in=c.tile_in,
+                                             sigma_multiplier=c.sigma_multiplier, normalize=c.normalize_gaussian,
+                                             clamp_quad=80.0)
+                return delta.view(m.out_features, m.in_features) * c.adapter_scale
+
+            m.compute_delta_weight = cdw
+
+    def render(self):
+        return None
+
+
 class DataParallelTrainer:
     """One data-parallel training step of the adapters (one process per GPU).
 

@@ -54,3 +54,28 @@ def test_bf16_training_steps(fused):
     # every adapter's mu_raw, chol_raw and amp receives a non-zero, finite gradient
     for p in tr.params:
         assert torch.isfinite(p.grad).all() and p.grad.abs().sum() > 0
+
+
+def test_per_layer_dropin_matches_batched_render_fp32(monkeypatch):
+    """Every layer rendering itself through the drop-in runtime (the
+    reference's call pattern) gives the loss and gradients of the batched
+    render with the same layer composition."""
+    monkeypatch.setattr(torch.backends.cudnn, "allow_tf32", False)
+    monkeypatch.setattr(torch.backends.cuda.matmul, "allow_tf32", False)
+    out = []
+    for mode in ("batched", "dropin"):
+        torch.manual_seed(0)
+        with torch.device("cuda"):
+            model = sd15.SD15UNet(sd15.tiny_config(), dtype=torch.float32)
+        model.cuda()
+        if mode == "dropin":
+            bank = sd15.PerLayerRender(model.adapters())
+        else:
+            bank = BatchedAdapters(model.adapters(), out_dtype=torch.float32)
+        bank.install()
+        tr = sd15.DataParallelTrainer(model, bank)
+        loss = tr.backward(sd15.synthetic_inputs(sd15.tiny_config(), 2, 3, device="cuda", dtype=torch.float32))
+        out.append((loss, _grads(model)))
+    torch.testing.assert_close(out[1][0], out[0][0], rtol=1e-5, atol=0)
+    for a, b in zip(out[1][1], out[0][1]):
+        torch.testing.assert_close(a, b, rtol=1e-4, atol=1e-7)
