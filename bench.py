@@ -332,11 +332,13 @@ def run_e2e_batched(w: UNetWorkload, steps: int, warmup: int, world: int):
 
 
 def run_e2e(w: UNetWorkload, steps: int, warmup: int, world: int):
-    """The same step through the drop-in per-layer API with host buffers."""
+    """The same step through the drop-in per-layer API with host buffers: per
+    layer, ``gaussian_field_train`` (what GaussianLinear calls in
+    cuda_field_train mode, gaussian_linear.py:178-190) forward, then its
+    autograd backward."""
     from guass_b200 import cuda_field
     from guass_b200.partition import all_gather_slots
 
-    ext = cuda_field.load_extension()
     host = []
     for i in w.own:
         f = w.fields[i]
@@ -349,16 +351,17 @@ def run_e2e(w: UNetWorkload, steps: int, warmup: int, world: int):
 
     def step():
         for i, h in zip(w.own, host):
-            mu = h["mu"].to("cuda", non_blocking=True)
-            chol = h["chol"].to("cuda", non_blocking=True)
-            amp = h["amp"].to("cuda", non_blocking=True)
-            delta, tp, ids = ext.gaussian_field_forward(h["row"], h["col"], mu, chol, amp, 32, 32, 3.0, False, 80.0)
-            w.layout.field_view(w.gathered, i).copy_(delta)  # the layer's bf16 weight dtype cast
+            mu = h["mu"].to("cuda", non_blocking=True).requires_grad_(True)
+            chol = h["chol"].to("cuda", non_blocking=True).requires_grad_(True)
+            amp = h["amp"].to("cuda", non_blocking=True).requires_grad_(True)
+            delta = cuda_field.gaussian_field_train(row_coords=h["row"], col_coords=h["col"], mu=mu, chol_raw=chol,
+                                                    amp=amp, tile_out=32, tile_in=32, sigma_multiplier=3.0,
+                                                    normalize=False, clamp_quad=80.0)
+            w.layout.field_view(w.gathered, i).copy_(delta.detach())  # the layer's bf16 weight dtype cast
             g = h["grad"].to("cuda", non_blocking=True)
-            grads = ext.gaussian_field_backward(g, h["row"], h["col"], mu, chol, amp, tp, ids, 32, 32, 3.0, False,
-                                                80.0)
-            for o, gr in zip(h["out"], grads):
-                o.copy_(gr, non_blocking=True)
+            delta.backward(g)
+            for o, p in zip(h["out"], (mu, chol, amp)):
+                o.copy_(p.grad, non_blocking=True)
         if world > 1:
             all_gather_slots(w.gathered, w.rank)
 
@@ -691,8 +694,9 @@ def main():
             e2e_ms, h2d, d2h = run_e2e(w, n_e2e, 2, world)
             e2e_layer = {"value": w.total_elements / (e2e_ms / 1e3), "unit": UNIT, "ms_per_step": e2e_ms,
                          "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-                         "path": "guass_b200.cuda_field per-layer drop-in API (the reference's call pattern: "
-                                 "128 calls, fp32 delta, one pair-count read per layer), pinned host params/grads"}
+                         "path": "guass_b200.cuda_field.gaussian_field_train per layer with its autograd backward "
+                                 "(what GaussianLinear calls; 128 renders, fp32 delta, binning kept on the device), "
+                                 "pinned host params/grads"}
         except Exception as exc:
             e2e_layer = {"error": f"{type(exc).__name__}: {exc}"}
 

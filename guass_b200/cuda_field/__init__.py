@@ -29,17 +29,40 @@ from guass_b200.cuda_field.runtime import (
 )
 
 
-def install() -> None:
+_ORIGINALS: dict = {}
+
+
+def install(train_runtime: bool = True) -> None:
     """Route ``gaussian_peft.cuda_field`` (if importable) through this renderer.
 
     The reference runtime binds ``load_extension`` by name at import
     (gaussian_peft/cuda_field/runtime.py:8), so both the loader module and the
-    runtime module are patched."""
+    runtime module are patched.  With ``train_runtime`` (default) the
+    training entry point is also this package's ``gaussian_field_train``,
+    which keeps the binning on the device (no pair-count read per layer);
+    GaussianLinear binds that name at import (gaussian_linear.py:11), so the
+    layer module's binding is replaced too.  :func:`uninstall` restores all."""
     import gaussian_peft.cuda_field.loader as ref_loader
     import gaussian_peft.cuda_field.runtime as ref_runtime
 
-    ref_loader.load_extension = load_extension
-    ref_runtime.load_extension = load_extension
+    targets = [(ref_loader, "load_extension", load_extension), (ref_runtime, "load_extension", load_extension)]
+    if train_runtime:
+        targets.append((ref_runtime, "gaussian_field_train", gaussian_field_train))
+        try:
+            import gaussian_peft.layers.gaussian_linear as ref_layer
+            targets.append((ref_layer, "gaussian_field_train", gaussian_field_train))
+        except ImportError:
+            pass
+    for mod, name, fn in targets:
+        _ORIGINALS.setdefault((mod.__name__, name), (mod, getattr(mod, name)))
+        setattr(mod, name, fn)
+
+
+def uninstall() -> None:
+    """Undo :func:`install`."""
+    for (_, name), (mod, fn) in list(_ORIGINALS.items()):
+        setattr(mod, name, fn)
+    _ORIGINALS.clear()
 
 
 __all__ = [
@@ -58,4 +81,5 @@ __all__ = [
     "get_source_paths",
     "install",
     "load_extension",
+    "uninstall",
 ]

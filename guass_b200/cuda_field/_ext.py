@@ -255,6 +255,81 @@ class GaussianFieldExtension:
                 raise_device_flags(ws)
         return [d_mu, d_chol, d_amp]
 
+    # Training path without host round trips.  The public forward must return
+    # gaussian_ids_sorted with exactly num_pairs entries, which costs one
+    # host read of the pair count per layer (the reference makes the same
+    # read, forward.cu:48-73).  The autograd training function only returns
+    # delta, so it can keep the binning in the library's shared-id form: ids
+    # in a buffer sized for the exact bound (every Gaussian in every tile --
+    # no overflow, no retry) and the pair count on the device (pair_base).
+    # Neither pass then reads anything back.  Same kernels and per-pair slot
+    # order as the public path, so the same delta and gradients.
+    def train_forward(self, row_coords, col_coords, mu, chol_raw, amp, tile_out, tile_in, sigma_multiplier,
+                      normalize, clamp_quad):
+        _validate_forward_inputs(row_coords, col_coords, mu, chol_raw, amp)
+        _check_config(tile_out, tile_in, sigma_multiplier)
+        device = mu.device
+        out_f, in_f, k = row_coords.numel(), col_coords.numel(), mu.size(0)
+        num_tiles = int(self._lib.gf_num_tiles(out_f, in_f, int(tile_out), int(tile_in)))
+        delta = torch.empty(out_f * in_f, dtype=torch.float32, device=device)
+        tile_ptr = torch.empty(num_tiles + 1, dtype=torch.int64, device=device)
+        pair_base = torch.zeros(2, dtype=torch.int64, device=device)
+        cap = k * num_tiles
+        ids = torch.empty(max(cap, 1), dtype=torch.int64, device=device)
+        cfg = make_config(tile_out, tile_in, sigma_multiplier, normalize, clamp_quad)
+        field = _lib.GfField(out_features=out_f, in_features=in_f, num_gaussians=k,
+                             row_coords=row_coords.data_ptr(), col_coords=col_coords.data_ptr(),
+                             mu=mu.data_ptr(), chol_raw=chol_raw.data_ptr(), amp=amp.data_ptr(),
+                             delta=delta.data_ptr(), tile_ptr=tile_ptr.data_ptr())
+        batch = _lib.GfBatch(num_fields=1, fields=ctypes.pointer(field), ids=ids.data_ptr(), ids_capacity=cap,
+                             pair_base=pair_base.data_ptr())
+        nbytes = self._lib.gf_workspace_bytes(ctypes.byref(cfg), ctypes.byref(batch), _lib.GF_PASS_FORWARD)
+        if nbytes == 0:
+            _lib.check(_lib.GF_ERR_INVALID_ARG)
+        with torch.cuda.device(device):
+            ws = _POOL.get(device, nbytes)
+            stream = torch.cuda.current_stream(device).cuda_stream
+            _lib.check(self._lib.gf_forward(ctypes.byref(cfg), ctypes.byref(batch), ws.data_ptr(), ws.numel(),
+                                            stream))
+            if _VALIDATE:
+                raise_device_flags(ws)
+        return delta, tile_ptr, ids, pair_base
+
+    def train_backward(self, grad_delta, row_coords, col_coords, mu, chol_raw, amp, tile_ptr, ids, pair_base,
+                       tile_out, tile_in, sigma_multiplier, normalize, clamp_quad):
+        _check_cuda(grad_delta, "grad_delta")
+        if grad_delta.dtype not in (torch.float32, torch.bfloat16):
+            raise RuntimeError("grad_delta must be float32")
+        out_f, in_f, k = row_coords.numel(), col_coords.numel(), mu.size(0)
+        if grad_delta.numel() != out_f * in_f:
+            raise RuntimeError("grad_delta must match flattened delta shape")
+        device = mu.device
+        d_mu = torch.empty(k, 2, dtype=torch.float32, device=device)
+        d_chol = torch.empty(k, 3, dtype=torch.float32, device=device)
+        d_amp = torch.empty(k, 1, dtype=torch.float32, device=device)
+        if k == 0:
+            return [d_mu, d_chol, d_amp]
+        gdt = _lib.GF_BF16 if grad_delta.dtype == torch.bfloat16 else _lib.GF_F32
+        cfg = make_config(tile_out, tile_in, sigma_multiplier, normalize, clamp_quad, grad_dtype=gdt)
+        field = _lib.GfField(out_features=out_f, in_features=in_f, num_gaussians=k,
+                             row_coords=row_coords.data_ptr(), col_coords=col_coords.data_ptr(),
+                             mu=mu.data_ptr(), chol_raw=chol_raw.data_ptr(), amp=amp.data_ptr(),
+                             tile_ptr=tile_ptr.data_ptr(), grad_delta=grad_delta.data_ptr(), d_mu=d_mu.data_ptr(),
+                             d_chol_raw=d_chol.data_ptr(), d_amp=d_amp.data_ptr())
+        batch = _lib.GfBatch(num_fields=1, fields=ctypes.pointer(field), ids=ids.data_ptr(),
+                             ids_capacity=ids.numel(), pair_base=pair_base.data_ptr())
+        nbytes = self._lib.gf_workspace_bytes(ctypes.byref(cfg), ctypes.byref(batch), _lib.GF_PASS_BACKWARD)
+        if nbytes == 0:
+            _lib.check(_lib.GF_ERR_INVALID_ARG)
+        with torch.cuda.device(device):
+            ws = _POOL.get(device, nbytes)
+            stream = torch.cuda.current_stream(device).cuda_stream
+            _lib.check(self._lib.gf_backward(ctypes.byref(cfg), ctypes.byref(batch), ws.data_ptr(), ws.numel(),
+                                             stream))
+            if _VALIDATE:
+                raise_device_flags(ws)
+        return [d_mu, d_chol, d_amp]
+
     # ext.cpp:73-110.  The reference routes this to an autograd replay of the
     # forward (backward.cu:500-539) whose result is meant to equal the train
     # backward; here it is the same exact backward.

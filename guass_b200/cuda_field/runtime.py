@@ -44,11 +44,40 @@ class _FieldFunctionBase(torch.autograd.Function):
 
 
 class GaussianFieldCudaTrainFunction(_FieldFunctionBase):
-    """The training path (runtime.py:107-203): explicit CUDA backward."""
+    """The training path (runtime.py:107-203): explicit CUDA backward.
+
+    With this package's extension the binning stays in the library's
+    shared-id form (``train_forward`` / ``train_backward``): the same kernels
+    and results, but no host read of the pair count per call, so a model's
+    layers render without a synchronisation each.  The saved state is then the
+    reference's seven tensors with the id buffer at its bound and the device
+    pair count appended.  Any other extension object (e.g. the reference's
+    own) is driven through the reference protocol."""
+
+    @staticmethod
+    def forward(ctx, row_coords: Tensor, col_coords: Tensor, mu: Tensor, chol_raw: Tensor, amp: Tensor,
+                tile_out: int, tile_in: int, sigma_multiplier: float, normalize: bool,
+                clamp_quad: float | None) -> Tensor:
+        ext = load_extension(verbose=False)
+        ctx.field_args = (tile_out, tile_in, sigma_multiplier, normalize, clamp_quad)
+        ctx.shared_ids = hasattr(ext, "train_forward")
+        if not ctx.shared_ids:
+            delta, tile_ptr, ids = ext.gaussian_field_forward(row_coords, col_coords, mu, chol_raw, amp, tile_out,
+                                                              tile_in, sigma_multiplier, normalize, clamp_quad)
+            ctx.save_for_backward(row_coords, col_coords, mu, chol_raw, amp, tile_ptr, ids)
+            return delta
+        delta, tile_ptr, ids, pair_base = ext.train_forward(row_coords, col_coords, mu, chol_raw, amp, tile_out,
+                                                            tile_in, sigma_multiplier, normalize, clamp_quad)
+        ctx.save_for_backward(row_coords, col_coords, mu, chol_raw, amp, tile_ptr, ids, pair_base)
+        return delta
 
     @staticmethod
     def backward(ctx, grad_delta: Tensor):
-        return GaussianFieldCudaTrainFunction._backward(ctx, grad_delta)
+        if not ctx.shared_ids:
+            return GaussianFieldCudaTrainFunction._backward(ctx, grad_delta)
+        ext = load_extension(verbose=False)
+        d_mu, d_chol_raw, d_amp = ext.train_backward(grad_delta.contiguous(), *ctx.saved_tensors, *ctx.field_args)
+        return None, None, d_mu, d_chol_raw, d_amp, None, None, None, None, None
 
 
 class GaussianFieldCudaReferenceFunction(_FieldFunctionBase):

@@ -20,7 +20,7 @@ gp = pytest.importorskip("gaussian_peft")
 from gaussian_peft.config.adapter import GaussianAdapterConfig  # noqa: E402
 from gaussian_peft.layers.gaussian_linear import GaussianLinear  # noqa: E402
 
-from test_adapters import OracleBatch  # noqa: E402
+from oracle_batch import OracleBatch  # noqa: E402
 
 from guass_b200 import cuda_field  # noqa: E402
 from guass_b200.adapters import BatchedAdapters, adapter_state_dict  # noqa: E402
@@ -30,19 +30,34 @@ def test_install_routes_reference_runtime_to_this_library():
     import gaussian_peft.cuda_field.loader as ref_loader
     import gaussian_peft.cuda_field.runtime as ref_runtime
 
-    saved = (ref_loader.load_extension, ref_runtime.load_extension)
+    import gaussian_peft.layers.gaussian_linear as ref_layer
+
+    saved = (ref_loader.load_extension, ref_runtime.load_extension, ref_runtime.gaussian_field_train,
+             ref_layer.gaussian_field_train)
+    args = dict(row_coords=torch.linspace(-1, 1, 8), col_coords=torch.linspace(-1, 1, 9), mu=torch.zeros(2, 2),
+                chol_raw=torch.zeros(2, 3), amp=torch.zeros(2, 1), tile_out=32, tile_in=32, sigma_multiplier=3.0)
     try:
-        cuda_field.install()
+        cuda_field.install(train_runtime=False)
         assert ref_runtime.load_extension is cuda_field.load_extension
         ext = ref_runtime.load_extension()
         assert type(ext).__module__ == "guass_b200.cuda_field._ext"
-        # the reference's train function now reaches our argument checks
-        args = dict(row_coords=torch.linspace(-1, 1, 8), col_coords=torch.linspace(-1, 1, 9), mu=torch.zeros(2, 2),
-                    chol_raw=torch.zeros(2, 3), amp=torch.zeros(2, 1), tile_out=32, tile_in=32, sigma_multiplier=3.0)
+        assert ref_layer.gaussian_field_train is saved[3]
+        # the reference's own train function now reaches our argument checks
         with pytest.raises(RuntimeError, match="row_coords must be a CUDA tensor"):
             ref_runtime.gaussian_field_train(**args)
+        cuda_field.uninstall()
+        cuda_field.install()  # default: the layers call this package's training function
+        assert ref_layer.gaussian_field_train is cuda_field.gaussian_field_train
+        assert ref_runtime.gaussian_field_train is cuda_field.gaussian_field_train
+        with pytest.raises(RuntimeError, match="row_coords must be a CUDA tensor"):
+            ref_layer.gaussian_field_train(**args)
+        cuda_field.uninstall()
+        assert (ref_loader.load_extension, ref_runtime.load_extension, ref_runtime.gaussian_field_train,
+                ref_layer.gaussian_field_train) == saved
     finally:
-        ref_loader.load_extension, ref_runtime.load_extension = saved
+        cuda_field.uninstall()
+        (ref_loader.load_extension, ref_runtime.load_extension, ref_runtime.gaussian_field_train,
+         ref_layer.gaussian_field_train) = saved
 
 
 def _layer(out_f, in_f, k, seed):
