@@ -299,6 +299,41 @@ class BatchedAdapters:
                     m.forward = orig[1]
 
 
+def gaussian_adapter_modules(model: nn.Module) -> dict:
+    """``{name: module}`` of every Gaussian adapter layer of ``model`` (modules
+    with ``mu_raw``, ``chol_raw``, ``amp`` and ``adapter_config``, i.e.
+    GUASS's GaussianLinear)."""
+    return {n: m for n, m in model.named_modules()
+            if all(hasattr(m, a) for a in ("mu_raw", "chol_raw", "amp", "adapter_config"))}
+
+
+class ModelRenderer:
+    """Every Gaussian adapter of ``model`` served by one batched render per
+    model forward (a forward pre-hook on ``model``), instead of one render per
+    layer inside each layer's forward (gaussian_linear.py:162-242).
+
+    After densify changes a layer's K the next forward rebuilds the binding.
+    ``remove()`` restores the layers' own rendering.  Keyword arguments go to
+    :class:`BatchedAdapters` (``out_dtype``, ``fused_weight``, ...)."""
+
+    def __init__(self, model: nn.Module, **kw):
+        mods = gaussian_adapter_modules(model)
+        if not mods:
+            raise ValueError("the model has no Gaussian adapter layers")
+        self.bank = BatchedAdapters(mods, **kw)
+        self.bank.install()
+        self._handle = model.register_forward_pre_hook(self._before_forward)
+
+    def _before_forward(self, module, args):
+        if self.bank.shapes_changed():
+            self.bank = self.bank.rebuilt()
+        self.bank.render()
+
+    def remove(self) -> None:
+        self._handle.remove()
+        self.bank.uninstall()
+
+
 def adapter_parameters(modules) -> list[torch.Tensor]:
     return [p for m in modules for p in (m.mu_raw, m.chol_raw, m.amp)]
 

@@ -99,3 +99,33 @@ def test_merge_into_reference_weights():
         bank.unmerge_weights()
         bank.uninstall()
     assert torch.allclose(layers["q"].weight, w0, atol=1e-7)
+
+
+def test_model_renderer_serves_a_reference_model():
+    """One batched render per model forward for a model of reference
+    GaussianLinear layers: same output and gradients as the layers' own path."""
+    from guass_b200.adapters import ModelRenderer
+
+    def model():
+        torch.manual_seed(0)
+        return torch.nn.Sequential(_layer(40, 64, 12, 0), torch.nn.GELU(), _layer(24, 40, 9, 1))
+
+    x = torch.randn(5, 64)
+    ref = model()
+    want = ref(x)
+    want.square().sum().backward()
+    m = model()
+    r = ModelRenderer(m, batch_factory=OracleBatch, out_dtype=torch.float32)
+    try:
+        got = m(x)
+        got.square().sum().backward()
+        assert r.bank.batch.calls == 1
+        torch.testing.assert_close(got, want, rtol=1e-4, atol=1e-6)
+        for a, b in zip(m.parameters(), ref.parameters()):
+            if b.grad is not None:
+                torch.testing.assert_close(a.grad, b.grad, rtol=1e-3, atol=1e-6)
+        m(x)
+        assert r.bank.batch.calls == 2  # one render per model forward
+    finally:
+        r.remove()
+    assert m[0].compute_delta_weight.__func__ is GaussianLinear.compute_delta_weight
