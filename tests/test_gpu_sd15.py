@@ -79,3 +79,30 @@ def test_per_layer_dropin_matches_batched_render_fp32(monkeypatch):
     torch.testing.assert_close(out[1][0], out[0][0], rtol=1e-5, atol=0)
     for a, b in zip(out[1][1], out[0][1]):
         torch.testing.assert_close(a, b, rtol=1e-4, atol=1e-7)
+
+
+def test_model_renderer_matches_per_layer_render_fp32(monkeypatch):
+    """ModelRenderer (one batched render per model forward, from a pre-hook)
+    gives the per-layer drop-in path's loss and gradients."""
+    from guass_b200.adapters import ModelRenderer
+
+    monkeypatch.setattr(torch.backends.cudnn, "allow_tf32", False)
+    monkeypatch.setattr(torch.backends.cuda.matmul, "allow_tf32", False)
+    inp = sd15.synthetic_inputs(sd15.tiny_config(), 2, 4, device="cuda", dtype=torch.float32)
+    out = []
+    for mode in ("dropin", "hook"):
+        torch.manual_seed(0)
+        with torch.device("cuda"):
+            model = sd15.SD15UNet(sd15.tiny_config(), dtype=torch.float32)
+        model.cuda()
+        if mode == "dropin":
+            sd15.PerLayerRender(model.adapters()).install()
+        else:
+            renderer = ModelRenderer(model, out_dtype=torch.float32)
+        loss = sd15.diffusion_loss(model, inp, sd15.noise_schedule("cuda"))
+        loss.backward()
+        out.append((loss.detach(), _grads(model)))
+    renderer.remove()
+    torch.testing.assert_close(out[1][0], out[0][0], rtol=1e-5, atol=0)
+    for a, b in zip(out[1][1], out[0][1]):
+        torch.testing.assert_close(a, b, rtol=1e-4, atol=1e-7)
