@@ -1,0 +1,60 @@
+"""Staged forward (gf_forward_stages) on one B200.
+
+BIN then RENDER equals gf_forward bit for bit; and the schedule the fused
+multi-GPU exchange uses -- binning, then the backward on a second stream
+(its own workspace) while the render runs -- gives the same delta and
+gradients as the plain sequence.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from guass_b200 import _lib, synthetic
+from guass_b200.batched import FieldBatch, pack_fields
+
+pytestmark = pytest.mark.gpu
+
+
+def _setup():
+    fields = synthetic.cfg3()[:24]
+    shapes = [(f.out_features, f.in_features, f.k) for f in fields]
+    mu, chol, amp, grad = pack_fields(fields, device="cuda")
+    cap = sum(k * -(-o // 32) * -(-i // 32) for o, i, k in shapes)
+    return shapes, (mu, chol, amp, grad), cap
+
+
+def test_stages_equal_the_full_forward():
+    shapes, (mu, chol, amp, grad), cap = _setup()
+    a = FieldBatch(shapes, ids_capacity=cap)
+    b = FieldBatch(shapes, ids_capacity=cap)
+    want = a.forward(mu, chol, amp).clone()
+    b.forward_stages(mu, chol, amp, _lib.GF_STAGE_BIN)
+    b.forward_stages(mu, chol, amp, _lib.GF_STAGE_RENDER)
+    assert torch.equal(b.delta, want)
+    assert torch.equal(b.tile_ptr, a.tile_ptr) and torch.equal(b.pair_base, a.pair_base)
+    assert a.device_flags() == 0 and b.device_flags() == 0
+
+
+def test_backward_overlapping_the_render_matches_the_sequence():
+    shapes, (mu, chol, amp, grad), cap = _setup()
+    seq = FieldBatch(shapes, ids_capacity=cap)
+    seq.forward(mu, chol, amp)
+    want_delta = seq.delta.clone()
+    want = [t.clone() for t in seq.backward(grad, mu, chol, amp)]
+
+    b = FieldBatch(shapes, ids_capacity=cap)
+    main = torch.cuda.current_stream()
+    side = torch.cuda.Stream()
+    for _ in range(3):  # repeated steps reuse both workspaces
+        b.forward_stages(mu, chol, amp, _lib.GF_STAGE_BIN, main)
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            got = b.backward(grad, mu, chol, amp, stream=side)
+        b.forward_stages(mu, chol, amp, _lib.GF_STAGE_RENDER, main)
+        main.wait_stream(side)
+        torch.cuda.synchronize()
+        assert torch.equal(b.delta, want_delta)
+        for g, w in zip(got, want):
+            assert torch.equal(g, w)
+    assert b.device_flags() == 0
