@@ -39,6 +39,9 @@ constexpr int kRenderThreads = 256;  // 8 warps; fast path tile = 32x32
 constexpr int kChunk = 256;          // candidate Gaussians tested per pass
 constexpr int kBinSmemCapInts = 24 * 1024;          // 96 KB diff array in smem
 constexpr int kBwdSmemCapFloats = 24 * 1024;        // 96 KB grad tile in smem
+// Cfg.flags bit set by the host for a RENDER-only stage: the BIN stage has
+// already written the per-tile id lists (emit_ids_kernel), the render does not.
+constexpr uint32_t kFlagIdsWritten = 0x80000000u;
 
 struct Cfg {
   int32_t tile_out, tile_in;
@@ -110,7 +113,7 @@ __device__ __forceinline__ bool gf_bounds_ok(bool ok, uint32_t* status) {
 }
 #define GF_IN_BOUNDS(cond) gf_bounds_ok((cond), p.status)
 #else
-#define GF_IN_BOUNDS(cond) true
+#define GF_IN_BOUNDS(cond) ((void)sizeof(cond), true)  // unevaluated: names its operands, costs nothing
 #endif
 
 // ---------------------------------------------------------------------------
@@ -363,6 +366,54 @@ bin_kernel(const __grid_constant__ Params<NF> p, int smem_cap_ints) {
 }
 
 // ---------------------------------------------------------------------------
+// BIN stage on its own (gf_forward_stages): the per-tile id lists, so that work
+// which reads them -- the backward -- can start before the render.  One warp
+// per tile tests the field's boxes 32 at a time by ballot, in ascending id
+// order: the same order and positions at which the render kernels write the
+// lists when they run the whole forward.
+constexpr int kEmitWarps = 4;
+
+template <int NF>
+__global__ void __launch_bounds__(32 * kEmitWarps) emit_ids_kernel(const __grid_constant__ Params<NF> p) {
+  const int tg = blockIdx.x * kEmitWarps + (threadIdx.x >> 5);
+  if (tg >= p.total_tiles) return;  // whole warps
+  const int lane = threadIdx.x & 31;
+  const int fi = field_of_tile(p, tg);
+  const DevField& F = p.f[fi];
+  const int t = tg - F.tile_base;
+  const int tr = t / F.ntc, tc = t % F.ntc;
+  const int64_t start = F.tile_ptr[t];
+  const int64_t count = F.tile_ptr[t + 1] - start;
+  int64_t* ids;
+  int64_t cap_left;
+  if (p.batch_ids != nullptr) {
+    const int64_t b = p.pair_base[fi];
+    ids = p.batch_ids + b + start;
+    cap_left = p.batch_cap - b - start;
+  } else {
+    ids = F.ids + start;
+    cap_left = F.ids_cap - start;
+  }
+  const int4* box = p.boxes + F.g_base;
+  int64_t found = 0;
+  for (int k0 = 0; k0 < F.K && found < count; k0 += 32) {
+    const int g = k0 + lane;
+    bool hit = false;
+    if (g < F.K && GF_IN_BOUNDS(F.g_base + g < p.total_g)) {
+      const int4 b = box[g];
+      hit = (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, hit);
+    if (hit) {
+      const int64_t pos = found + __popc(m & ((1u << lane) - 1u));
+      if (pos < cap_left) ids[pos] = g;
+    }
+    found += __popc(m);
+  }
+  if (lane == 0 && found != count) atomicOr(p.status, GF_FLAG_INTERNAL);
+}
+
+// ---------------------------------------------------------------------------
 // Forward kernel 2: tile render, one CTA (8 warps) per tile.
 //
 // Work is split into 32x32 sub-blocks (one for the default tile).  Lane =
@@ -439,7 +490,7 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
         if (hit) {
           const int pos = before + __popc(m & ((1u << lane) - 1u));
           s_list[pos] = g;
-          if (first && found + pos < cap_left) ids[found + pos] = g;
+          if (first && found + pos < cap_left && !(p.cfg.flags & kFlagIdsWritten)) ids[found + pos] = g;
         }
         __syncthreads();
         if (tid < total) {
@@ -640,7 +691,7 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
       hit = (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
     }
     unsigned m = __ballot_sync(0xffffffffu, hit);
-    if (warp == 0 && hit) {
+    if (warp == 0 && hit && !(p.cfg.flags & kFlagIdsWritten)) {
       const int64_t pos = found + __popc(m & ((1u << lane) - 1u));
       if (pos < cap_left) ids[pos] = g;
     }
@@ -1436,9 +1487,15 @@ gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout&
     trace_mark(st);
     bin_kernel<NF><<<p.n, kBinThreads, smem, st>>>(p, kBinSmemCapInts);
     GF_LAUNCH_CHECK("bin_kernel");
+    if (!(stages & GF_STAGE_RENDER)) {
+      // the BIN stage alone also writes the id lists (the render normally does)
+      emit_ids_kernel<NF><<<(int)ceil_div(L.total_tiles, kEmitWarps), 32 * kEmitWarps, 0, st>>>(p);
+      GF_LAUNCH_CHECK("emit_ids_kernel");
+    }
     trace_mark(st);
   }
   if (!(stages & GF_STAGE_RENDER)) return GF_OK;
+  if (!(stages & GF_STAGE_BIN)) p.cfg.flags |= kFlagIdsWritten;
   NvtxRange r("gfield.render_fwd");
   const bool norm = p.cfg.normalize, clamp = p.cfg.has_clamp;
   const int grid = (int)L.total_tiles;

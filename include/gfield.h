@@ -193,7 +193,9 @@ int gf_trace_count(void);
  * (== gf_forward).  A RENDER stage must follow a BIN stage of the same batch,
  * parameters and workspace, in stream order.  Work that needs only the
  * binning -- gf_backward on another stream with its own workspace -- may
- * start once the BIN stage is complete, so that it overlaps the render.
+ * start once the BIN stage is complete, so that it overlaps the render.  (A
+ * BIN stage run alone also writes the per-tile id lists, which gf_forward
+ * leaves to its render kernel: one extra small launch.)
  * Trace events: BIN records 2 (start, bin), RENDER 1 (render). */
 gf_status gf_forward_stages(const gf_config* cfg, const gf_batch* batch, void* workspace, size_t workspace_bytes,
                             unsigned stages, gf_stream stream);

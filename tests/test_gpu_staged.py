@@ -1,9 +1,10 @@
 """Staged forward (gf_forward_stages) on one B200.
 
 BIN then RENDER equals gf_forward bit for bit; and the schedule the fused
-multi-GPU exchange uses -- binning, then the backward on a second stream
-(its own workspace) while the render runs -- gives the same delta and
-gradients as the plain sequence.
+multi-GPU exchange uses -- binning (which, run alone, also writes the
+per-tile id lists), then the backward on a second stream (its own workspace)
+while the render runs -- gives the same delta and gradients as the plain
+sequence.
 """
 from __future__ import annotations
 
@@ -44,6 +45,7 @@ def test_backward_overlapping_the_render_matches_the_sequence():
     want = [t.clone() for t in seq.backward(grad, mu, chol, amp)]
 
     b = FieldBatch(shapes, ids_capacity=cap)
+    b.ids.fill_(-7)  # any id the backward reads must come from the BIN stage, not from a racing render
     main = torch.cuda.current_stream()
     side = torch.cuda.Stream()
     for _ in range(3):  # repeated steps reuse both workspaces
