@@ -49,15 +49,18 @@ def _capacity_kw(shapes, tile_out, tile_in):
 class BatchedFieldFunction(torch.autograd.Function):
     """Packed render of every field of ``batch``.
 
-    ``batch`` provides ``forward(mu, chol_raw, amp) -> delta`` and
+    ``batch`` provides ``forward(mu, chol_raw, amp, out=...) -> delta`` and
     ``backward(grad, mu, chol_raw, amp) -> (d_mu, d_chol_raw, d_amp)``
-    (:class:`guass_b200.batched.FieldBatch`).  The returned delta is the
-    batch's own output buffer: it stays valid until the batch renders again."""
+    (:class:`guass_b200.batched.FieldBatch`).  Every render writes a fresh
+    output tensor: a graph that saved an earlier render's delta (a second
+    model forward before the backward, gradient accumulation) keeps its own
+    values.  The caching allocator hands the freed buffer back, so in a
+    one-forward-per-step loop this costs nothing."""
 
     @staticmethod
     def forward(ctx, batch, mu, chol_raw, amp):
         mu, chol_raw, amp = mu.contiguous(), chol_raw.contiguous(), amp.contiguous()
-        delta = batch.forward(mu, chol_raw, amp)
+        delta = batch.forward(mu, chol_raw, amp, out=torch.empty_like(batch.delta))
         ctx.batch = batch
         ctx.save_for_backward(mu, chol_raw, amp)
         return delta

@@ -96,6 +96,7 @@ class FieldBatch:
         self._ws_bwd = None  # backward workspace (separate, so a backward may overlap a render)
         self._bound = None
         self._grad_bound = None
+        self._out_bound = None
         self._fields = (_lib.GfField * n)()
         self._batch = _lib.GfBatch(num_fields=n, fields=ctypes.cast(self._fields, ctypes.POINTER(_lib.GfField)))
         self.base_weight = None
@@ -180,7 +181,7 @@ class FieldBatch:
             fd.mu = mu.data_ptr() + 8 * g0
             fd.chol_raw = chol_raw.data_ptr() + 12 * g0
             fd.amp = amp.data_ptr() + 4 * g0
-            fd.delta = self.delta.data_ptr() + esz_out * n0
+            fd.delta = self.delta.data_ptr() + esz_out * n0  # rebound per call by _bind_out
             fd.tile_ptr = self.tile_ptr.data_ptr() + 8 * self.t_off[f]
             fd.gaussian_ids = None
             fd.ids_capacity = 0
@@ -199,21 +200,41 @@ class FieldBatch:
         if self._ws_bwd is None or self._ws_bwd.numel() < need_b:
             self._ws_bwd = torch.zeros(need_b, dtype=torch.uint8, device=self.device)
         self._bound = key
+        self._out_bound = self.delta.data_ptr()  # the loop above pointed every field at self.delta
 
     # -- passes --------------------------------------------------------------
-    def forward(self, mu, chol_raw, amp, stream=None) -> torch.Tensor:
-        """Render every field into ``self.delta``; no host synchronisation."""
-        return self.forward_stages(mu, chol_raw, amp, _lib.GF_STAGE_BIN | _lib.GF_STAGE_RENDER, stream)
+    def forward(self, mu, chol_raw, amp, stream=None, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Render every field into ``self.delta`` (or into ``out``, a packed
+        tensor like it, e.g. a fresh one per call so that earlier results stay
+        intact); no host synchronisation."""
+        return self.forward_stages(mu, chol_raw, amp, _lib.GF_STAGE_BIN | _lib.GF_STAGE_RENDER, stream, out)
 
-    def forward_stages(self, mu, chol_raw, amp, stages: int, stream=None) -> torch.Tensor:
+    def forward_stages(self, mu, chol_raw, amp, stages: int, stream=None,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
         """``forward`` in stages (GF_STAGE_BIN, GF_STAGE_RENDER): a backward
         that needs only this step's binning may start on another stream once
         the BIN stage is done and overlap the RENDER stage."""
         self._bind(mu, chol_raw, amp)
+        dst = self._bind_out(out)
         st = (stream or torch.cuda.current_stream(self.device)).cuda_stream
         _lib.check(self._lib.gf_forward_stages(ctypes.byref(self.cfg), ctypes.byref(self._batch), self._ws.data_ptr(),
                                                self._ws.numel(), int(stages), st))
-        return self.delta
+        return dst
+
+    def _bind_out(self, out):
+        dst = self.delta if out is None else out
+        if out is not None and (out.dtype != self.out_dtype or not out.is_contiguous() or out.numel() != self.numel()
+                                or out.device != self.device):
+            raise RuntimeError(f"out must be a contiguous {self.out_dtype} tensor of {self.numel()} elements on "
+                               f"{self.device}")
+        if self.delta_multicast and out is not None:
+            raise RuntimeError("out= cannot be combined with delta_multicast (the multicast buffer is fixed)")
+        if dst.data_ptr() != self._out_bound:
+            esz = dst.element_size()
+            for f in range(len(self.shapes)):
+                self._fields[f].delta = dst.data_ptr() + esz * self.n_off[f]
+            self._out_bound = dst.data_ptr()
+        return dst
 
     def backward(self, grad, mu, chol_raw, amp, stream=None):
         """dL/d(delta) (packed, grad_dtype) -> (d_mu, d_chol_raw, d_amp) packed."""

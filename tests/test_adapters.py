@@ -332,3 +332,19 @@ def test_render_publishes_layer_metadata():
     quiet = _modules()
     BatchedAdapters(quiet, batch_factory=OracleBatch, track_metadata=False).render()
     assert not hasattr(quiet["a"], "last_forward_metadata")
+
+
+def test_each_render_returns_its_own_delta():
+    """A later render (here after a parameter change) must not overwrite the
+    delta an earlier render returned: a graph that saved it keeps its values."""
+    mods = _modules()
+    bank = BatchedAdapters(mods, batch_factory=OracleBatch)
+    first = bank.render()
+    kept = [d.detach().clone() for d in first]
+    with torch.no_grad():
+        for m in mods.values():
+            m.amp.mul_(3.0)
+    second = bank.render()
+    for a, b, c in zip(first, kept, second):
+        assert torch.equal(a.detach(), b)
+        assert not torch.equal(c.detach(), b)
