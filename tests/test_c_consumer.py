@@ -34,6 +34,17 @@ int main(void) {
   if (gf_forward(&cfg, &b, NULL, 0, NULL) != GF_ERR_INVALID_ARG) return 6;
   if (strcmp(gf_last_error(), "tile_out must be positive") != 0) return 7;
   if (gf_multicast_store(NULL, NULL, 16, 1, NULL) != GF_ERR_INVALID_ARG) return 8;
+  /* extensions: staged forward, densify statistics (argument errors, host side) */
+  cfg.tile_out = 32;
+  if (gf_forward_stages(&cfg, &b, NULL, 0, 0u, NULL) != GF_ERR_INVALID_ARG) return 9;
+  if (gf_forward_stages(&cfg, &b, NULL, 0, GF_STAGE_BIN | 4u, NULL) != GF_ERR_INVALID_ARG) return 10;
+  gf_stats_layer layer;
+  memset(&layer, 0, sizeof(layer));
+  layer.num_gaussians = 8; /* stats missing */
+  if (gf_grad_stats_accumulate(1, &layer, NULL) != GF_ERR_INVALID_ARG) return 11;
+  if (gf_grad_stats_accumulate(0, NULL, NULL) != GF_OK) return 12;
+  cfg.flags = GF_CFG_BWD_EXP2; /* an option bit is accepted by the host checks */
+  if (gf_workspace_bytes(&cfg, &b, GF_PASS_BACKWARD) == 0) return 13;
   printf("ok %zu %zu\n", fwd, bwd);
   return 0;
 }
