@@ -13,7 +13,6 @@ fp64 sum and the covariance chain the same way.  So these hold bit for bit.
 from __future__ import annotations
 
 import numpy as np
-import torch
 
 
 def _f32(t):

@@ -12,7 +12,6 @@ import os
 import socket
 from dataclasses import dataclass
 
-import numpy as np
 import pytest
 import torch
 import torch.distributed as dist

@@ -6,14 +6,13 @@ by an ulp or two); gradients within 1e-5 of their channel scale + 1e-7.
 """
 from __future__ import annotations
 
-import math
 
 import numpy as np
 import pytest
 import torch
 
 from guass_b200 import synthetic as S
-from gpu_helpers import (ATOL, RTOL, assert_grad_close, assert_grads_exact_within, exact_grads, random_field,
+from gpu_helpers import (ATOL, RTOL, assert_grads_exact_within, exact_grads, random_field,
                          run_ext, run_oracle)
 
 pytestmark = pytest.mark.gpu

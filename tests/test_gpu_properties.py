@@ -4,7 +4,6 @@ batch (cfg3, 128 fields, 93.5 M delta elements) and the 1280x1280 K=1024
 field (cfg2)."""
 from __future__ import annotations
 
-import numpy as np
 import pytest
 import torch
 

@@ -11,7 +11,6 @@ They are skipped when the reference build is not present.
 """
 from __future__ import annotations
 
-import math
 
 import numpy as np
 import pytest
