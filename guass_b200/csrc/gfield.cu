@@ -1326,6 +1326,7 @@ gf_status validate(const gf_config* cfg, const gf_batch* batch, gf_pass pass, bo
   if (!(cfg->sigma_multiplier > 0.0)) return fail(GF_ERR_INVALID_ARG, "sigma_multiplier must be positive");
   if (cfg->out_dtype != GF_F32 && cfg->out_dtype != GF_BF16) return fail(GF_ERR_INVALID_ARG, "out_dtype must be GF_F32 or GF_BF16");
   if (cfg->grad_dtype != GF_F32 && cfg->grad_dtype != GF_BF16) return fail(GF_ERR_INVALID_ARG, "grad_dtype must be GF_F32 or GF_BF16");
+  if (cfg->flags & ~GF_CFG_BWD_EXP2) return fail(GF_ERR_INVALID_ARG, "unknown gf_config.flags bits 0x%x", cfg->flags);
   if (batch->num_fields < 1 || batch->num_fields > GF_MAX_FIELDS)
     return fail(GF_ERR_INVALID_ARG, "num_fields must be in [1, %d], got %d", GF_MAX_FIELDS, batch->num_fields);
   if (!batch->fields) return fail(GF_ERR_INVALID_ARG, "fields must be non-null");

@@ -115,6 +115,7 @@ def test_workspace_bytes():
     (dict(tile_in=-1), 1, "tile_in must be positive"),
     (dict(sigma_multiplier=0.0), 1, "sigma_multiplier must be positive"),
     (dict(out_dtype=7), 1, "out_dtype"),
+    (dict(flags=0x80000000), 1, "unknown gf_config.flags"),
     ({}, 0, "num_fields"),
     ({}, _lib.GF_MAX_FIELDS + 1, "num_fields"),
 ])
