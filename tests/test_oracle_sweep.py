@@ -27,6 +27,7 @@ pytest.importorskip("gaussian_peft")
 
 import oracle  # noqa: E402
 from guass_b200.synthetic import make_field  # noqa: E402
+from sweep_configs import draw  # noqa: E402
 
 
 def _ref(f, to, ti, sigma, norm, clamp):
@@ -47,16 +48,9 @@ def _ref(f, to, ti, sigma, norm, clamp):
 
 @pytest.mark.parametrize("seed", range(24))
 def test_oracle_vs_reference_torch_random_config(seed):
-    rng = np.random.default_rng(1000 + seed)
-    out_f, in_f = int(rng.integers(1, 130)), int(rng.integers(1, 130))
-    k = int(rng.integers(1, 40))
-    to, ti = int(rng.choice([8, 16, 32, 13, 64])), int(rng.choice([8, 16, 32, 7, 64]))
-    sigma = float(rng.choice([1.5, 2.0, 3.0, 4.5]))
-    norm = bool(rng.integers(0, 2))
-    clamp = [80.0, None, 20.0][int(rng.integers(0, 3))]
-    f = make_field(out_f, in_f, k, seed=seed, log_scale_mean=math.log(float(rng.choice([0.03, 0.1, 0.3]))),
-                   log_scale_std=0.6, elongated_frac=float(rng.choice([0.0, 0.5])))
-    kw = dict(tile_out=to, tile_in=ti, sigma_multiplier=sigma, normalize=norm, clamp_quad=clamp)
+    f, kw = draw(seed)
+    to, ti, sigma, norm, clamp = (kw["tile_out"], kw["tile_in"], kw["sigma_multiplier"], kw["normalize"],
+                                  kw["clamp_quad"])
     from gaussian_peft.kernels.covariance import activate_cholesky
     L = activate_cholesky(f.chol_raw.double(), eps=1e-5)
     det = (L[:, 0, 0] * L[:, 1, 1]).square()
