@@ -76,6 +76,9 @@ def parse_args():
     ap.add_argument("--bwd-exp", choices=["expf", "ex2"], default="expf",
                     help="backward basis: CUDA expf (default) or the base-2 hardware approximation "
                          "(GF_CFG_BWD_EXP2; the forward's delta is bit-exact either way)")
+    ap.add_argument("--fwd-exp", choices=["expf", "ex2"], default="expf",
+                    help="bf16 forward basis: CUDA expf (default: RNE of the reference's fp32 sum) or the base-2 "
+                         "hardware approximation (GF_CFG_FWD_EXP2, within the bf16 tolerance)")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
     return a
@@ -166,7 +169,8 @@ def sum_over_ranks(x: float, world: int) -> float:
 class UNetWorkload:
     """Fields of the whole UNet, partitioned; this rank's batch and buffers."""
 
-    def __init__(self, rank: int, world: int, exchange: str = "auto", groups: int = 4, bwd_exp2: bool = False):
+    def __init__(self, rank: int, world: int, exchange: str = "auto", groups: int = 4, bwd_exp2: bool = False,
+                 fwd_exp2: bool = False):
         from guass_b200 import synthetic
         from guass_b200.batched import FieldBatch, pack_fields
         from guass_b200.partition import PartitionedRenderer, field_costs
@@ -189,7 +193,8 @@ class UNetWorkload:
         del full, mu, chol, amp
         use_mc = {"auto": False, "multicast": True, "fused": True, "nccl": False}[exchange]
         self.renderer = PartitionedRenderer(shapes, self.costs, rank, world, groups=groups, use_multicast=use_mc,
-                                            fused=(exchange == "fused"), bwd_exp2=bwd_exp2)
+                                            fused=(exchange == "fused"), bwd_exp2=bwd_exp2,
+                                            fwd_exp2=fwd_exp2)
         self.parts, self.own = self.renderer.parts, self.renderer.own
         self.layout, self.gathered = self.renderer.layout, self.renderer.gathered
         own_fields = [self.fields[i] for i in self.own]
@@ -406,10 +411,21 @@ def interleaved_order(n=128, stride=16):
     return [i for s in range(stride) for i in range(s, n, stride)]
 
 
+def host_threads() -> int:
+    """Every host core this process may run on.  Set explicitly: under
+    torch.distributed.run OMP_NUM_THREADS defaults to 1, which would time the
+    CPU path single-threaded at N > 1."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_baseline(fields, budget_s):
     import oracle
 
     oracle.build()
+    oracle.set_threads(host_threads())
     threads = oracle.max_threads()
     el, t, names = cpu_oracle_sample(fields, budget_s, interleaved_order(len(fields)))
     return {"value": el / t, "unit": UNIT, "cores": threads, "kind": "port",
@@ -427,6 +443,7 @@ def reference_arm(a, rank, world):
     import oracle
 
     oracle.build()
+    oracle.set_threads(host_threads())
     fields = synthetic.cfg3()
     order = interleaved_order(len(fields))
     per_step = max(1, len(fields) // 16)
@@ -655,7 +672,7 @@ def main():
         reference_arm(a, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))
         return
     rank, world, local = setup_dist()
-    w = UNetWorkload(rank, world, a.exchange, a.groups, bwd_exp2=(a.bwd_exp == "ex2"))
+    w = UNetWorkload(rank, world, a.exchange, a.groups, bwd_exp2=(a.bwd_exp == "ex2"), fwd_exp2=(a.fwd_exp == "ex2"))
     sampler = ClockSampler() if local == 0 else None
     if sampler:
         sampler.start()
@@ -729,6 +746,7 @@ def main():
                    "elements": w.total_elements, "pairs": w.total_pairs, "evals": w.total_evals,
                    "delta_dtype": "bf16", "grad_dtype": "f32", "tile": "32x32", "sigma_multiplier": 3.0,
                    "backward_basis": "ex2.approx" if a.bwd_exp == "ex2" else "expf",
+                   "forward_basis": "ex2.approx" if a.fwd_exp == "ex2" else "expf",
                    "clamp_quad": 80.0, "partition": f"LPT by render cost over {world} rank(s)",
                    "parallelism": f"layer-partition x{world} + {w.renderer.exchange} of bf16 delta "
                                   f"({len(w.renderer.batches)} field groups)" if world > 1 else "single GPU",

@@ -35,6 +35,7 @@ GF_PASS_FORWARD = 0
 GF_PASS_BACKWARD = 1
 
 GF_CFG_BWD_EXP2 = 0x1
+GF_CFG_FWD_EXP2 = 0x2
 GF_STAGE_BIN = 1
 GF_STAGE_RENDER = 2
 GF_FLAG_CAPACITY = 0x1

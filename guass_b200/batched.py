@@ -44,7 +44,7 @@ class FieldBatch:
                  grad_dtype=torch.float32, out_scale: float = 1.0, device="cuda", ids_capacity: int | None = None,
                  row_coords=None, col_coords=None, delta_out: torch.Tensor | None = None,
                  base_weight: torch.Tensor | None = None, delta_multicast: int | None = None,
-                 bwd_exp2: bool = False):
+                 bwd_exp2: bool = False, fwd_exp2: bool = False):
         self.shapes = [s if isinstance(s, FieldShape) else FieldShape(*s) for s in shapes]
         n = len(self.shapes)
         if not 1 <= n <= _lib.GF_MAX_FIELDS:
@@ -56,10 +56,12 @@ class FieldBatch:
         self.tile_out, self.tile_in = int(tile_out), int(tile_in)
         self.out_dtype, self.grad_dtype = out_dtype, grad_dtype
         self.out_scale = float(out_scale)
-        # bwd_exp2: backward basis from the base-2 hardware approximation (GF_CFG_BWD_EXP2)
+        # bwd_exp2 / fwd_exp2: backward basis / bf16 forward basis from the base-2 hardware
+        # approximation (GF_CFG_BWD_EXP2 / GF_CFG_FWD_EXP2); tolerance-bound, not bit-exact
+        flags = (_lib.GF_CFG_BWD_EXP2 if bwd_exp2 else 0) | (_lib.GF_CFG_FWD_EXP2 if fwd_exp2 else 0)
         self.cfg = make_config(tile_out, tile_in, sigma_multiplier, normalize, clamp_quad,
                                out_dtype=_DT[out_dtype], grad_dtype=_DT[grad_dtype], out_scale=out_scale,
-                               flags=_lib.GF_CFG_BWD_EXP2 if bwd_exp2 else 0)
+                               flags=flags)
         self._lib = _lib.lib()
         L = self._lib
         self.num_tiles = [int(L.gf_num_tiles(s.out_features, s.in_features, tile_out, tile_in)) for s in self.shapes]

@@ -24,6 +24,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -590,6 +591,14 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
   }
 }
 
+// Hardware base-2 exponential (MUFU.EX2, ftz): a few 1e-7 relative error.
+constexpr float kLog2e = 1.44269504088896340736f;
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 // ---------------------------------------------------------------------------
 // Packed fp32x2 arithmetic (sm_100: one issue slot for two IEEE fp32
 // operations, each rounded exactly like the scalar instruction).
@@ -641,7 +650,7 @@ __device__ __forceinline__ f2 sub2(f2 a, f2 b) {
 #endif
 constexpr int kFwd32Warps = GF_FWD32_WARPS;
 
-template <int NF, bool NORM, bool CLAMP, int OUTT>
+template <int NF, bool NORM, bool CLAMP, int OUTT, bool EX2>
 __global__ void __launch_bounds__(32 * kFwd32Warps)
 render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
   constexpr int R = 32 / kFwd32Warps;  // rows per warp
@@ -696,6 +705,40 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
       if (pos < cap_left) ids[pos] = g;
     }
     found += __popc(m);
+    if (EX2) {
+      // bf16 output (GF_CFG_FWD_EXP2): the form in base 2 with the column
+      // terms hoisted, q2 = dx*(g00*dx + 2*g01*dy) + g11*dy^2 (g = log2e*h),
+      // and the basis 2^q2 from MUFU.EX2; the normalisation folds into the
+      // amplitude.  Relative error per term ~1e-5 at worst (cancelling terms
+      // of very elongated Gaussians), far below bf16's 3.9e-3 ulp.
+      while (m) {
+        const int gg = k0 + __ffs(m) - 1;
+        m &= m - 1;
+        const float4 a = rec[2 * gg];
+        const float4 h = rec[2 * gg + 1];
+        const float dy = cc - a.y;
+        const float g00 = h.x * kLog2e, g01 = h.y * kLog2e, g11 = h.z * kLog2e;
+        const f2 G00 = pk2(g00, g00);
+        const float b1 = 2.0f * g01 * dy, c0 = g11 * dy * dy;
+        const f2 B1 = pk2(b1, b1), C0 = pk2(c0, c0), MUR = pk2(a.x, a.x);
+        const float ampn = NORM ? a.z * a.w : a.z;
+        const f2 AMP = pk2(ampn, ampn);
+        const float nclamp2 = nclamp * kLog2e;
+#pragma unroll
+        for (int i = 0; i < R / 2; ++i) {
+          const f2 DX = sub2(CR[i], MUR);
+          const f2 Q = fma2(DX, fma2(G00, DX, B1), C0);
+          float q0, q1;
+          up2(Q, q0, q1);
+          if (CLAMP) {
+            q0 = fmaxf(q0, nclamp2);
+            q1 = fmaxf(q1, nclamp2);
+          }
+          V[i] = fma2(AMP, pk2(ex2_approx(q0), ex2_approx(q1)), V[i]);
+        }
+      }
+      continue;
+    }
     while (m) {
       const int gg = k0 + __ffs(m) - 1;
       m &= m - 1;
@@ -867,12 +910,19 @@ __device__ __forceinline__ float load_grad(const void* g, size_t i) {
 // The tile's dL/d(delta) is read from HBM once into shared memory (the
 // reference re-reads it once per pair, backward.cu:301-308).  Warp i handles
 // the tile's pairs i, i+8, ...; lane = column, so dy is fixed per lane and the
-// per-element work is the basis plus four running sums:
-//   T0 = sum g*b,  U0 = sum g*b*[q active],  U1 = sum .. *dx,  U2 = sum .. *dx^2
-// from which the reference's per-pair channels follow exactly in real
-// arithmetic (backward.cu:330-351, with A01 == A10):
-//   amp: T0                  mu0: A00*U1 + A01*dy*U0   mu1: A01*U1 + A11*dy*U0
-//   A00: U2   A01 = A10: dy*U1   A11: dy^2*U0      (times amp, -0.5 later)
+// per-element work is the basis plus six running sums (gba = g*b where the
+// q-gradient is active, 0 where the form is clamped):
+//   T0 = sum g*b,  U0 = sum gba,  U1 = sum gba*dx,  U2 = sum gba*dx^2,
+//   M0 = sum gba*(h00*dx + h01*dy),  M1 = sum gba*(h01*dx + h11*dy)
+// (h = -0.5*A), from which the reference's per-pair channels follow
+// (backward.cu:330-351, with A01 == A10):
+//   amp: T0    mu0: -2*M0    mu1: -2*M1
+//   A00: U2    A01 = A10: dy*U1    A11: dy^2*U0      (times amp, -0.5 later)
+// The mu factors are evaluated per element with the reference's roundings:
+// for an elongated Gaussian A00*dx and A01*dy nearly cancel, and a sum
+// factored as A00*U1 + A01*dy*U0 would carry their rounding, not that of the
+// (much smaller) per-element terms.  The A factors carry no such cancellation
+// (dy is exact per lane), so they stay factored.
 // Lanes are reduced with a fixed xor-shuffle tree and lane 0 writes the six
 // channels to the pair's slot, goff[g] + (its tile's index in g's box), so the
 // finalize kernel reads each Gaussian's pairs contiguously.
@@ -938,34 +988,46 @@ render_bwd_kernel(const __grid_constant__ Params<NF> p) {
       const float dy = cval ? __fsub_rn(cc, a.y) : 0.0f;
       const float a01 = __fmul_rn(h.y, dy);
       const float a11 = __fmul_rn(h.z, dy);
-      float T0 = 0.f, U0 = 0.f, U1 = 0.f, U2 = 0.f;
+      // running sums: [0] T0, [1] U0, [2] U1, [3] U2, [4] M0, [5] M1; rows are
+      // summed in blocks of 8 and the blocks added, so the rounding error grows
+      // with 8 + th/8 terms instead of th
+      float acc[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       const float* gcol = s_g + (cval ? c : 0);
-      for (int r = 0; r < th; ++r) {
-        const float dx = __fsub_rn(s_row[r], a.x);
-        float q = quad_scaled(dx, dy, h.x, a01, h.y, a11);
-        q = fminf(q, 0.0f);
-        bool act = true;
-        if (CLAMP) {
-          act = q > nclamp;          // reference: quad < clamp
-          q = fmaxf(q, nclamp);
+      for (int r8 = 0; r8 < th; r8 += 8) {
+        float blk[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        const int rend = min(th, r8 + 8);
+        for (int r = r8; r < rend; ++r) {
+          const float dx = __fsub_rn(s_row[r], a.x);
+          float q = quad_scaled(dx, dy, h.x, a01, h.y, a11);
+          q = fminf(q, 0.0f);
+          bool act = true;
+          if (CLAMP) {
+            act = q > nclamp;          // reference: quad < clamp
+            q = fmaxf(q, nclamp);
+          }
+          float e = expf(q);
+          if (NORM) e = __fmul_rn(e, a.w);
+          const float gb = __fmul_rn(cval ? gcol[r * TI] : 0.0f, e);
+          const float gba = act ? gb : 0.0f;
+          blk[0] = __fadd_rn(blk[0], gb);
+          blk[1] = __fadd_rn(blk[1], gba);
+          blk[2] = __fmaf_rn(gba, dx, blk[2]);
+          blk[3] = __fmaf_rn(__fmul_rn(gba, dx), dx, blk[3]);
+          // the reference's per-element mu factors (backward.cu:338-340),
+          // -0.25*dq/dmu with its roundings: h00*dx + h01*dy, h01*dx + h11*dy
+          blk[4] = __fmaf_rn(gba, __fadd_rn(__fmul_rn(h.x, dx), a01), blk[4]);
+          blk[5] = __fmaf_rn(gba, __fadd_rn(__fmul_rn(h.y, dx), a11), blk[5]);
         }
-        float e = expf(q);
-        if (NORM) e = __fmul_rn(e, a.w);
-        const float gb = (cval ? gcol[r * TI] : 0.0f) * e;
-        T0 += gb;
-        const float gba = act ? gb : 0.0f;
-        U0 += gba;
-        U1 = fmaf(gba, dx, U1);
-        U2 = fmaf(gba * dx, dx, U2);
+#pragma unroll
+        for (int k = 0; k < 6; ++k) acc[k] = __fadd_rn(acc[k], blk[k]);
       }
-      const float i00 = -2.0f * h.x, i01 = -2.0f * h.y, i11 = -2.0f * h.z;
-      const float dyU0 = dy * U0;
-      ch[0] += T0;
-      ch[1] += i00 * U1 + i01 * dyU0;
-      ch[2] += i01 * U1 + i11 * dyU0;
-      ch[3] += U2;
-      ch[4] += dy * U1;
-      ch[5] += dy * dyU0;
+      const float dyU0 = __fmul_rn(dy, acc[1]);
+      ch[0] = __fadd_rn(ch[0], acc[0]);
+      ch[1] = __fadd_rn(ch[1], -2.0f * acc[4]);
+      ch[2] = __fadd_rn(ch[2], -2.0f * acc[5]);
+      ch[3] = __fadd_rn(ch[3], acc[3]);
+      ch[4] = __fadd_rn(ch[4], __fmul_rn(dy, acc[2]));
+      ch[5] = __fadd_rn(ch[5], __fmul_rn(dy, dyU0));
     }
 #pragma unroll
     for (int k = 0; k < 6; ++k) ch[k] = warp_sum(ch[k]);
@@ -1005,7 +1067,7 @@ render_bwd_kernel(const __grid_constant__ Params<NF> p) {
 constexpr int kBwd32Warps = GF_BWD32_WARPS;
 
 struct PairSums {
-  f2 T0, U0, U1, U2;
+  f2 T0, U0, U1, U2, M0, M1;
 };
 
 // Sum over the 32 rows of one lane's column for one pair.
@@ -1016,18 +1078,13 @@ struct PairSums {
 // ex2.approx adds a few 1e-7.  Every gradient term keeps its relative
 // accuracy to ~3e-7, inside the backward's tolerance.  The forward always
 // uses CUDA's expf, which the bit parity of delta requires.
-constexpr float kLog2e = 1.44269504088896340736f;
-__device__ __forceinline__ float exp_via_ex2(float q) {
-  float r;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(__fmul_rn(q, kLog2e)));
-  return r;
-}
+__device__ __forceinline__ float exp_via_ex2(float q) { return ex2_approx(__fmul_rn(q, kLog2e)); }
 
 template <bool NORM, bool TRACK_CLAMP, bool EX2>
 __device__ __forceinline__ PairSums bwd32_pair_rows(const float* s_rows, const float* s_gcol, f2 H00, f2 H01,
                                                    f2 A01, f2 A11, f2 DY, f2 MUR, float nclamp, float nf) {
   const f2 zero2 = pk2(0.0f, 0.0f);
-  PairSums S{zero2, zero2, zero2, zero2};
+  PairSums S{zero2, zero2, zero2, zero2, zero2, zero2};
 #pragma unroll
   for (int k = 0; k < 16; ++k) {
     const float2 rr = *reinterpret_cast<const float2*>(&s_rows[2 * k]);
@@ -1070,6 +1127,9 @@ __device__ __forceinline__ PairSums bwd32_pair_rows(const float* s_rows, const f
     S.U0 = add2(S.U0, GBA);
     S.U1 = fma2(GBA, DX, S.U1);
     S.U2 = fma2(mul2(GBA, DX), DX, S.U2);
+    // per-element mu factors with the reference's roundings (see render_bwd_kernel)
+    S.M0 = fma2(GBA, add2(mul2(H00, DX), A01), S.M0);
+    S.M1 = fma2(GBA, add2(mul2(H01, DX), A11), S.M1);
   }
   if (!TRACK_CLAMP) S.T0 = S.U0;
   return S;
@@ -1160,15 +1220,17 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
     }
     PairSums S = track ? bwd32_pair_rows<NORM, true, EX2>(s_rows, s_gcol, H00, H01, A01, A11, DY, MUR, nclamp, a.w)
                        : bwd32_pair_rows<NORM, false, EX2>(s_rows, s_gcol, H00, H01, A01, A11, DY, MUR, nclamp, a.w);
-    float t0a, t0b, u0a, u0b, u1a, u1b, u2a, u2b;
+    float t0a, t0b, u0a, u0b, u1a, u1b, u2a, u2b, m0a, m0b, m1a, m1b;
     up2(S.T0, t0a, t0b);
     up2(S.U0, u0a, u0b);
     up2(S.U1, u1a, u1b);
     up2(S.U2, u2a, u2b);
-    const float t0 = t0a + t0b, u0 = u0a + u0b, u1 = u1a + u1b, u2 = u2a + u2b;
-    const float i00 = -2.0f * h.x, i01 = -2.0f * h.y, i11 = -2.0f * h.z;
-    const float dyU0 = dy * u0;
-    float ch[8] = {t0, i00 * u1 + i01 * dyU0, i01 * u1 + i11 * dyU0, u2, dy * u1, dy * dyU0, 0.0f, 0.0f};
+    up2(S.M0, m0a, m0b);
+    up2(S.M1, m1a, m1b);
+    const float u0 = __fadd_rn(u0a, u0b), u1 = __fadd_rn(u1a, u1b);
+    const float dyU0 = __fmul_rn(dy, u0);
+    float ch[8] = {__fadd_rn(t0a, t0b), -2.0f * __fadd_rn(m0a, m0b), -2.0f * __fadd_rn(m1a, m1b),
+                   __fadd_rn(u2a, u2b), __fmul_rn(dy, u1), __fmul_rn(dy, dyU0), 0.0f, 0.0f};
     // reduce-scatter over the warp: 8 -> 4 -> 2 -> 1 channels, then 4-lane sums
     {
       const bool hi = (lane >> 4) & 1;
@@ -1326,7 +1388,7 @@ gf_status validate(const gf_config* cfg, const gf_batch* batch, gf_pass pass, bo
   if (!(cfg->sigma_multiplier > 0.0)) return fail(GF_ERR_INVALID_ARG, "sigma_multiplier must be positive");
   if (cfg->out_dtype != GF_F32 && cfg->out_dtype != GF_BF16) return fail(GF_ERR_INVALID_ARG, "out_dtype must be GF_F32 or GF_BF16");
   if (cfg->grad_dtype != GF_F32 && cfg->grad_dtype != GF_BF16) return fail(GF_ERR_INVALID_ARG, "grad_dtype must be GF_F32 or GF_BF16");
-  if (cfg->flags & ~GF_CFG_BWD_EXP2) return fail(GF_ERR_INVALID_ARG, "unknown gf_config.flags bits 0x%x", cfg->flags);
+  if (cfg->flags & ~(GF_CFG_BWD_EXP2 | GF_CFG_FWD_EXP2)) return fail(GF_ERR_INVALID_ARG, "unknown gf_config.flags bits 0x%x", cfg->flags);
   if (batch->num_fields < 1 || batch->num_fields > GF_MAX_FIELDS)
     return fail(GF_ERR_INVALID_ARG, "num_fields must be in [1, %d], got %d", GF_MAX_FIELDS, batch->num_fields);
   if (!batch->fields) return fail(GF_ERR_INVALID_ARG, "fields must be non-null");
@@ -1464,6 +1526,24 @@ void fill_params(Params<NF>& P, const gf_config* cfg, const gf_batch* batch, con
     if (e_ != cudaSuccess) return fail(GF_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e_)); \
   } while (0)
 
+// Opt a kernel in to more than 48 KB of dynamic shared memory.  The attribute
+// is per device, so it is set once per (kernel, device), under a per-kernel
+// flag array that concurrent host threads may race on harmlessly (setting it
+// twice is idempotent).  Devices beyond the table get the call every time.
+constexpr int kAttrDevices = 64;
+template <auto Kernel>
+cudaError_t allow_dynamic_smem(int bytes) {
+  static std::atomic<int> done[kAttrDevices];
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const bool tracked = dev >= 0 && dev < kAttrDevices;
+  if (tracked && done[dev].load(std::memory_order_acquire) == bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && tracked) done[dev].store(bytes, std::memory_order_release);
+  return e;
+}
+
 template <int NF>
 gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout& L, char* ws, cudaStream_t st,
                       unsigned stages = GF_STAGE_BIN | GF_STAGE_RENDER) {
@@ -1478,10 +1558,9 @@ gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout&
     if (nd <= kBinSmemCapInts && nd > max_nd) max_nd = nd;
   }
   const size_t smem = sizeof(int) * (size_t)max_nd;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(bin_kernel<NF>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBinSmemCapInts * 4);
-    attr_set = true;
+  {
+    const cudaError_t e = allow_dynamic_smem<bin_kernel<NF>>(kBinSmemCapInts * 4);
+    if (e != cudaSuccess) return fail(GF_ERR_CUDA, "bin_kernel: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   }
   if (stages & GF_STAGE_BIN) {
     NvtxRange r("gfield.bin");
@@ -1502,7 +1581,9 @@ gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout&
   const int grid = (int)L.total_tiles;
 #define GF_FWD(N, C, O)                                                                         \
   do {                                                                                          \
-    if (fast32) render_fwd32_kernel<NF, N, C, O><<<grid, 32 * kFwd32Warps, 0, st>>>(p);         \
+    if (fast32 && O == GF_BF16 && (p.cfg.flags & GF_CFG_FWD_EXP2))                               \
+      render_fwd32_kernel<NF, N, C, O, (O == GF_BF16)><<<grid, 32 * kFwd32Warps, 0, st>>>(p);   \
+    else if (fast32) render_fwd32_kernel<NF, N, C, O, false><<<grid, 32 * kFwd32Warps, 0, st>>>(p); \
     else render_fwd_kernel<NF, N, C, O><<<grid, kRenderThreads, 0, st>>>(p);                    \
   } while (0)
   const bool fast32 = cfg->tile_out == 32 && cfg->tile_in == 32;
@@ -1520,19 +1601,16 @@ gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout&
 }
 
 template <int NF, bool N, bool C, int G>
-void launch_bwd_render(const Params<NF>& p, int grid, size_t smem, cudaStream_t st) {
+cudaError_t launch_bwd_render(const Params<NF>& p, int grid, size_t smem, cudaStream_t st) {
   if (p.cfg.tile_out == 32 && p.cfg.tile_in == 32) {
     if (p.cfg.flags & GF_CFG_BWD_EXP2) render_bwd32_kernel<NF, N, C, G, true><<<grid, 32 * kBwd32Warps, 0, st>>>(p);
     else render_bwd32_kernel<NF, N, C, G, false><<<grid, 32 * kBwd32Warps, 0, st>>>(p);
-    return;
+    return cudaSuccess;
   }
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(render_bwd_kernel<NF, N, C, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         kBwdSmemCapFloats * 4);
-    attr_set = true;
-  }
+  const cudaError_t e = allow_dynamic_smem<render_bwd_kernel<NF, N, C, G>>(kBwdSmemCapFloats * 4);
+  if (e != cudaSuccess) return e;
   render_bwd_kernel<NF, N, C, G><<<grid, kRenderThreads, smem, st>>>(p);
+  return cudaSuccess;
 }
 
 template <int NF>
@@ -1552,7 +1630,8 @@ gf_status run_backward(const gf_config* cfg, const gf_batch* batch, const Layout
   const int grid = (int)L.total_tiles;
   const size_t smem = sizeof(float) * ((size_t)cfg->tile_out * cfg->tile_in + cfg->tile_out);
   NvtxRange r("gfield.render_bwd+finalize");
-#define GF_BWD(N, C, G) launch_bwd_render<NF, N, C, G>(p, grid, smem, st)
+  cudaError_t attr_err = cudaSuccess;
+#define GF_BWD(N, C, G) attr_err = launch_bwd_render<NF, N, C, G>(p, grid, smem, st)
   if (cfg->grad_dtype == GF_F32) {
     if (norm) { if (clamp) GF_BWD(true, true, GF_F32); else GF_BWD(true, false, GF_F32); }
     else { if (clamp) GF_BWD(false, true, GF_F32); else GF_BWD(false, false, GF_F32); }
@@ -1561,6 +1640,8 @@ gf_status run_backward(const gf_config* cfg, const gf_batch* batch, const Layout
     else { if (clamp) GF_BWD(false, true, GF_BF16); else GF_BWD(false, false, GF_BF16); }
   }
 #undef GF_BWD
+  if (attr_err != cudaSuccess)
+    return fail(GF_ERR_CUDA, "render_bwd_kernel: cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
   GF_LAUNCH_CHECK("render_bwd_kernel");
   trace_mark(st);
   if (L.total_g > 0) {
@@ -1801,7 +1882,9 @@ gf_status noalloc_launch(Params<NF>& p, const gf_config* cfg, const gf_batch* ba
   const int grid = (int)L.total_tiles;
 #define GF_FWD(N, C, O)                                                                         \
   do {                                                                                          \
-    if (fast32) render_fwd32_kernel<NF, N, C, O><<<grid, 32 * kFwd32Warps, 0, st>>>(p);         \
+    if (fast32 && O == GF_BF16 && (p.cfg.flags & GF_CFG_FWD_EXP2))                               \
+      render_fwd32_kernel<NF, N, C, O, (O == GF_BF16)><<<grid, 32 * kFwd32Warps, 0, st>>>(p);   \
+    else if (fast32) render_fwd32_kernel<NF, N, C, O, false><<<grid, 32 * kFwd32Warps, 0, st>>>(p); \
     else render_fwd_kernel<NF, N, C, O><<<grid, kRenderThreads, 0, st>>>(p);                    \
   } while (0)
   const bool fast32 = cfg->tile_out == 32 && cfg->tile_in == 32;

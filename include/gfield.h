@@ -86,6 +86,12 @@ typedef struct gf_config {
  * expf (a few 1e-7 relative per term; the backward is tolerance-bound, the
  * forward's delta stays bit-exact either way). */
 #define GF_CFG_BWD_EXP2 0x1u
+/* gf_config.flags: with out_dtype == GF_BF16 and 32x32 tiles, the forward
+ * evaluates its basis in base 2 with the hardware approximation (relative
+ * error per term well below bf16's rounding; results within the bf16
+ * tolerance of the reference, not bit-identical to RNE of its fp32 sum).
+ * fp32 outputs and other tile shapes keep the reference's expf. */
+#define GF_CFG_FWD_EXP2 0x2u
 
 /* One field (layer).  Forward reads the inputs and writes delta, tile_ptr and
  * (in per-field id mode) gaussian_ids; backward reads grad_delta, tile_ptr and
@@ -242,12 +248,17 @@ gf_status gf_grad_stats_accumulate(int32_t num_layers, const gf_stats_layer* lay
  * 4 MiB array inside the library instead, held by every GPU that loads the
  * library until the process exits.  Batches whose forward scratch
  * (gf_workspace_bytes(cfg, batch, GF_PASS_FORWARD)) exceeds
- * GF_NOALLOC_SCRATCH_BYTES are rejected with GF_ERR_UNSUPPORTED; in per-field
- * id mode a caller detects an id buffer that was too small by reading
- * tile_ptr[T] (the pair count) after the call.  The first call on a device
- * looks up the array's device address on that device, so make it before any
- * stream capture.  All calls share the one array: calls whose work overlaps
- * on the GPU race on it and must be ordered by the caller. */
+ * GF_NOALLOC_SCRATCH_BYTES are rejected with GF_ERR_UNSUPPORTED.  The
+ * device status bits of gf_workspace_status() stay inside the array, so a
+ * caller detects an id buffer that was too small from the pair counts: in
+ * per-field id mode tile_ptr[T] > ids_capacity, in shared-id mode
+ * pair_base[num_fields] > ids_capacity (then the ids, not delta, are
+ * truncated).  The first call on a device looks up the array's device
+ * address on that device and keeps it for the life of the process, so make
+ * it before any stream capture, and do not use this entry point on a device
+ * after cudaDeviceReset() (the kept address would be stale).  All calls
+ * share the one array: calls whose work overlaps on the GPU race on it and
+ * must be ordered by the caller. */
 gf_status gf_forward_noalloc(const gf_config* cfg, const gf_batch* batch, gf_stream stream);
 
 #ifdef __cplusplus

@@ -62,10 +62,12 @@ def _load():
     lib.gfo_backward.restype = None
     _D = ctypes.POINTER(ctypes.c_double)
     lib.gfo_backward_f64.argtypes = [_i64, _i64, _i64, _i64, _i64, _d, _F, _F, _F, _F, _F, _F, _I, _I, _i64,
-                                     _int, _int, _d, _D, _D, _D, _D, _D, _D]
+                                     _int, _int, _d, _D, _D, _D, _D, _D, _D, _F, _F]
     lib.gfo_backward_f64.restype = None
     lib.gfo_max_threads.argtypes = []
     lib.gfo_max_threads.restype = _int
+    lib.gfo_set_threads.argtypes = [_int]
+    lib.gfo_set_threads.restype = None
     _lib = lib
     return lib
 
@@ -169,10 +171,15 @@ def backward(grad_delta, row_coords, col_coords, mu, chol_raw, amp, tile_ptr, ga
 
 
 def backward_f64(grad_delta, row_coords, col_coords, mu, chol_raw, amp, tile_ptr, gaussian_ids_sorted,
-                 tile_out=32, tile_in=32, sigma_multiplier=3.0, normalize=False, clamp_quad=80.0):
+                 tile_out=32, tile_in=32, sigma_multiplier=3.0, normalize=False, clamp_quad=80.0, geometry=None):
     """Checker backward: exact (double) reductions and chain on the reference's
     float per-element terms.  Returns ((d_mu, d_chol_raw, d_amp), (S_mu, S_chol_raw, S_amp))
-    where S is the same computation on absolute values (the conditioning scale)."""
+    where S is the same computation on absolute values (the conditioning scale).
+
+    ``geometry`` = (inv_cov [K,2,2] float32, det [K] float32) evaluates the
+    terms with a device's own preprocess instead of the host's (the host's
+    log1pf/expf may differ from CUDA's by an ulp; the det cancellation of an
+    elongated Gaussian turns that into ~1e-5 of its inverse covariance)."""
     lib = _load()
     grad = _f32(grad_delta).reshape(-1)
     row = _f32(row_coords)
@@ -186,13 +193,22 @@ def backward_f64(grad_delta, row_coords, col_coords, mu, chol_raw, amp, tile_ptr
     outs = [np.zeros((k, 2)), np.zeros((k, 3)), np.zeros(k), np.zeros((k, 2)), np.zeros((k, 3)), np.zeros(k)]
     ids_buf = ids if ids.size else np.zeros(1, np.int64)
     P = ctypes.POINTER(ctypes.c_double)
+    g_inv = g_det = None
+    if geometry is not None:
+        g_inv = _f32(geometry[0]).reshape(-1)
+        g_det = _f32(geometry[1]).reshape(-1)
+        if g_inv.size != 4 * k or g_det.size != k:
+            raise ValueError("geometry must be (inv_cov [K,2,2], det [K])")
     lib.gfo_backward_f64(row.shape[0], col.shape[0], k, tile_out, tile_in, float(sigma_multiplier), _pf(grad),
                          _pf(row), _pf(col), _pf(mu), _pf(chol_raw), _pf(amp), _pi(tile_ptr), _pi(ids_buf),
                          ids.size, int(bool(normalize)), int(clamp_quad is not None), float(clamp_quad or 0.0),
-                         *[o.ctypes.data_as(P) for o in outs])
+                         *[o.ctypes.data_as(P) for o in outs],
+                         _pf(g_inv) if g_inv is not None else None, _pf(g_det) if g_det is not None else None)
     return (outs[0], outs[1], outs[2].reshape(k, 1)), (outs[3], outs[4], outs[5].reshape(k, 1))
 
 
 def set_threads(n: int) -> None:
-    """Set the OpenMP thread count for subsequent calls (before first use)."""
+    """Set the OpenMP thread count of subsequent calls (any time, through the
+    library; the environment variable alone is read only once, at start-up)."""
     os.environ["OMP_NUM_THREADS"] = str(int(n))
+    _load().gfo_set_threads(int(n))

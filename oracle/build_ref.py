@@ -27,7 +27,8 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 REF_OUT = HERE / "_ref"
 MODULE_NAME = "gaussian_peft_cuda_field_reference"  # loader.py:10-11
-DEFAULT_SRC = "/root/reference"
+# GUASS project root (the reference sources); override with GUASS_REFERENCE_ROOT
+DEFAULT_SRC = os.environ.get("GUASS_REFERENCE_ROOT", "/root/reference")
 
 
 def build(src_root: str = DEFAULT_SRC, verbose: bool = False) -> Path | None:

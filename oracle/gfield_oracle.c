@@ -44,6 +44,14 @@ int gfo_max_threads(void) {
 #endif
 }
 
+void gfo_set_threads(int n) {
+#ifdef _OPENMP
+  if (n >= 1) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
+
 /* forward.cu:25-27 (softplus_stable_scalar). */
 static float softplus_stable(float x) {
   return log1pf(expf(-fabsf(x))) + fmaxf(x, 0.0f);
@@ -402,7 +410,8 @@ void gfo_backward_f64(int64_t out_features, int64_t in_features, int64_t k,
                       int64_t num_pairs, int normalize, int has_clamp_quad,
                       double clamp_quad, double* d_mu, double* d_chol_raw,
                       double* d_amp, double* s_mu, double* s_chol_raw,
-                      double* s_amp) {
+                      double* s_amp, const float* geo_inv,
+                      const float* geo_det) {
   const int64_t ntr = (out_features + tile_out - 1) / tile_out;
   const int64_t ntc = (in_features + tile_in - 1) / tile_in;
   const int64_t num_tiles = ntr * ntc;
@@ -412,6 +421,8 @@ void gfo_backward_f64(int64_t out_features, int64_t in_features, int64_t k,
   gfo_preprocess(out_features, in_features, k, tile_out, tile_in,
                  sigma_multiplier, mu, chol_raw, inv, det, box, box + k,
                  box + 2 * k, box + 3 * k, box + 4 * k);
+  if (geo_inv) memcpy(inv, geo_inv, sizeof(float) * (size_t)(k * 4));
+  if (geo_det) memcpy(det, geo_det, sizeof(float) * (size_t)k);
   int64_t* pair_tile = (int64_t*)malloc(sizeof(int64_t) * (size_t)(num_pairs + 1));
   for (int64_t t = 0; t < num_tiles; ++t)
     for (int64_t p = tile_ptr[t]; p < tile_ptr[t + 1] && p < num_pairs; ++p)

@@ -61,7 +61,11 @@ void gfo_backward(int64_t out_features, int64_t in_features, int64_t k,
                   float* d_amp);
 
 /* Checker variant: double reductions and chain, plus summand magnitudes
- * S (same shapes as the gradients) for condition-aware tolerances. */
+ * S (same shapes as the gradients) for condition-aware tolerances.
+ * geo_inv [K,4] / geo_det [K], when non-NULL, replace the host-computed
+ * inverse covariance and det (for example with a device's own preprocess:
+ * its log1pf/expf may differ from the host's by an ulp, which the det
+ * cancellation of an elongated Gaussian amplifies to ~1e-5 of the inverse). */
 void gfo_backward_f64(int64_t out_features, int64_t in_features, int64_t k,
                       int64_t tile_out, int64_t tile_in, double sigma_multiplier,
                       const float* grad, const float* row_coords,
@@ -71,10 +75,13 @@ void gfo_backward_f64(int64_t out_features, int64_t in_features, int64_t k,
                       int64_t num_pairs, int normalize, int has_clamp_quad,
                       double clamp_quad, double* d_mu, double* d_chol_raw,
                       double* d_amp, double* s_mu, double* s_chol_raw,
-                      double* s_amp);
+                      double* s_amp, const float* geo_inv, const float* geo_det);
 
 /* Threads used by the OpenMP loops (1 when built without OpenMP). */
 int gfo_max_threads(void);
+
+/* Set the OpenMP thread count of subsequent calls (n >= 1). */
+void gfo_set_threads(int n);
 
 #ifdef __cplusplus
 }

@@ -6,6 +6,7 @@ library and the C oracle are (re)built here if their sources are newer.
 """
 from __future__ import annotations
 
+import os
 import sys
 from pathlib import Path
 
@@ -14,6 +15,10 @@ import pytest
 ROOT = Path(__file__).resolve().parent.parent
 if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
+
+# GUASS project root with the reference sources (tests that import or build
+# the reference skip when it is absent, as on the GPU box)
+REFERENCE_ROOT = os.environ.get("GUASS_REFERENCE_ROOT", "/root/reference")
 
 
 def pytest_configure(config):

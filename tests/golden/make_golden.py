@@ -16,6 +16,7 @@ Usage:  python tests/golden/make_golden.py [--reference /root/reference]
 from __future__ import annotations
 
 import argparse
+import os
 import math
 import sys
 from pathlib import Path
@@ -72,7 +73,7 @@ def run_case(name, spec, seed=0):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("GUASS_REFERENCE_ROOT", "/root/reference"))
     a = ap.parse_args()
     sys.path.insert(0, a.reference)
     torch.set_num_threads(1)

@@ -10,7 +10,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from gpu_helpers import ATOL, RTOL, assert_grads_exact_within, exact_grads, run_ext, run_oracle
+from gpu_helpers import ATOL, RTOL, assert_grads_exact_within, exact_grads, grad_errors, run_ext, run_oracle
 from sweep_configs import draw
 
 pytestmark = pytest.mark.gpu
@@ -32,3 +32,47 @@ def test_cuda_vs_oracle_random_config(seed):
     atol = max(ATOL, 2e-6 * float(np.abs(d_o).max()))
     np.testing.assert_allclose(d_g, d_o, rtol=RTOL, atol=atol)
     assert_grads_exact_within(gr_g, exact_grads(f, tp_o, ids_o, **args), label=f"sweep:{seed}")
+
+
+@pytest.fixture(scope="module")
+def ref_ext():
+    try:
+        from oracle import build_ref
+        return build_ref.load()
+    except (FileNotFoundError, ImportError, OSError) as e:
+        pytest.skip(f"reference extension not available: {e}")
+
+
+def _worst_over_bound(grads, exact):
+    """Largest err / bound over the three gradient tensors (<= 1 is within the bound)."""
+    truth, scales = exact
+    w = 0.0
+    for got, t, sc in zip(grads, truth, scales):
+        err, bound = grad_errors(got, t, sc)
+        if err.size:
+            w = max(w, float((err / bound).max()))
+    return w
+
+
+@pytest.mark.parametrize("seed", range(24))
+def test_gradients_no_farther_from_exact_than_reference_extension(ref_ext, seed):
+    """On every sweep configuration, this build's gradients are at least as
+    close to the fp64 evaluation of the reference's per-element terms as the
+    reference extension's own gradients on the same inputs and binning
+    (measured as the worst error in units of the tolerance bound; both below
+    a tenth of the bound counts as a tie)."""
+    import torch
+
+    f, kw = draw(seed)
+    args = dict(tile_out=kw["tile_out"], tile_in=kw["tile_in"], sigma=kw["sigma_multiplier"],
+                normalize=kw["normalize"], clamp=kw["clamp_quad"])
+    _, tp, ids, mine = run_ext(f, **args)
+    d = f.to("cuda")
+    tpd, idsd = torch.from_numpy(tp).cuda(), torch.from_numpy(ids).cuda()
+    theirs = ref_ext.gaussian_field_backward(d.grad, d.row_coords, d.col_coords, d.mu, d.chol_raw, d.amp, tpd, idsd,
+                                             kw["tile_out"], kw["tile_in"], kw["sigma_multiplier"], kw["normalize"],
+                                             kw["clamp_quad"])
+    theirs = [t.cpu().numpy() for t in theirs]
+    exact = exact_grads(f, tp, ids, **args)
+    w_mine, w_ref = _worst_over_bound(mine, exact), _worst_over_bound(theirs, exact)
+    assert w_mine <= max(w_ref, 0.1), f"seed {seed}: worst err/bound {w_mine:.3g} vs reference {w_ref:.3g}"

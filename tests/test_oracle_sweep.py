@@ -20,7 +20,7 @@ import numpy as np
 import pytest
 import torch
 
-REF = "/root/reference"
+from conftest import REFERENCE_ROOT as REF  # noqa: E402
 if REF not in sys.path:
     sys.path.append(REF)
 pytest.importorskip("gaussian_peft")

@@ -12,7 +12,7 @@ import sys
 import pytest
 import torch
 
-REF = "/root/reference"
+from conftest import REFERENCE_ROOT as REF  # noqa: E402
 if REF not in sys.path:
     sys.path.append(REF)
 gp = pytest.importorskip("gaussian_peft")

@@ -18,7 +18,7 @@ def test_cuda_only_no_cpu_path():
 
 
 def test_interface_matches_reference_tracker():
-    ref_root = "/root/reference"
+    from conftest import REFERENCE_ROOT as ref_root
     if ref_root not in sys.path:
         sys.path.append(ref_root)
     stats = pytest.importorskip("gaussian_peft.controllers.stats")

@@ -24,7 +24,6 @@ from guass_b200.cuda_field._ext import make_config
 
 pytestmark = pytest.mark.gpu
 
-RTOL, ATOL = 1e-5, 1e-7
 
 
 def _batch(fields, cfg):
@@ -81,11 +80,13 @@ def _run_noalloc(fields, cfg, bf16=False):
 
 
 def _assert_same(got, want):
+    # both entry points launch the same kernels on the same inputs: the
+    # outputs must be identical bit for bit
     for (d, tp, ids), (d0, tp0, ids0) in zip(got, want):
         np.testing.assert_array_equal(tp, tp0)
         np.testing.assert_array_equal(ids, ids0)
         assert np.isfinite(d).all()
-        np.testing.assert_allclose(d, d0, rtol=RTOL, atol=ATOL)
+        np.testing.assert_array_equal(d.view(np.uint32), d0.view(np.uint32))
 
 
 def test_noalloc_matches_workspace_forward_two_calls_in_a_row():
@@ -108,7 +109,51 @@ def test_noalloc_bf16_and_normalize():
     for (d, tp, ids), (d0, tp0, ids0) in zip(got, want):
         np.testing.assert_array_equal(tp, tp0)
         np.testing.assert_array_equal(ids, ids0)
-        np.testing.assert_allclose(d, d0, rtol=1e-2, atol=ATOL)
+        np.testing.assert_array_equal(d.view(np.uint32), d0.view(np.uint32))
+
+
+def _shared_batch(fields, cfg):
+    """Shared-id mode: every field's pairs go into one id buffer at pair_base[f]."""
+    L = _lib.lib()
+    b, descs, keep = _batch(fields, cfg)
+    cap = sum(f.k * int(L.gf_num_tiles(f.out_features, f.in_features, cfg.tile_out, cfg.tile_in)) for f in fields)
+    ids = torch.full((max(cap, 1),), -7, dtype=torch.int64, device="cuda")
+    pair_base = torch.full((len(fields) + 1,), -7, dtype=torch.int64, device="cuda")
+    for d in descs:
+        d.gaussian_ids, d.ids_capacity = None, 0
+    b.ids, b.ids_capacity, b.pair_base = ids.data_ptr(), cap, pair_base.data_ptr()
+    return b, descs, keep, ids, pair_base
+
+
+def _run_shared(fields, cfg, noalloc):
+    L = _lib.lib()
+    b, descs, keep, ids, pair_base = _shared_batch(fields, cfg)
+    st = torch.cuda.current_stream().cuda_stream
+    if noalloc:
+        _lib.check(L.gf_forward_noalloc(ctypes.byref(cfg), ctypes.byref(b), st))
+    else:
+        n = L.gf_workspace_bytes(ctypes.byref(cfg), ctypes.byref(b), _lib.GF_PASS_FORWARD)
+        ws = torch.zeros(n, dtype=torch.uint8, device="cuda")
+        _lib.check(L.gf_forward(ctypes.byref(cfg), ctypes.byref(b), ws.data_ptr(), n, st))
+    torch.cuda.synchronize()
+    pb = pair_base.cpu().numpy()
+    return ([(out["delta"].cpu().numpy(), out["tile_ptr"].cpu().numpy()) for _, out in keep], pb,
+            ids.cpu().numpy()[:pb[-1]])
+
+
+def test_noalloc_shared_ids_two_calls_in_a_row():
+    """Shared-id mode uses the scratch header's completion counter (the last
+    binning CTA writes pair_base); a second call must find it reset."""
+    cfg = make_config(32, 32, 3.0, False, 80.0)
+    fields = [synthetic.cfg1(), synthetic.make_field(64, 96, 40, seed=9), synthetic.cfg0()]
+    want = _run_shared(fields, cfg, noalloc=False)
+    for _ in range(2):
+        got = _run_shared(fields, cfg, noalloc=True)
+        np.testing.assert_array_equal(got[1], want[1])
+        np.testing.assert_array_equal(got[2], want[2])
+        for (d, tp), (d0, tp0) in zip(got[0], want[0]):
+            np.testing.assert_array_equal(tp, tp0)
+            np.testing.assert_array_equal(d.view(np.uint32), d0.view(np.uint32))
 
 
 def test_noalloc_rejects_batches_beyond_the_static_scratch():
