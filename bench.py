@@ -48,8 +48,6 @@ METRIC = "Gaussian-field dW fwd+bwd elements/s (whole SD1.5 UNet, 128 projection
 UNIT = "elements/s"
 # FMA-pipe operations per (element, Gaussian) evaluation, per the survey's
 # roofline definition (forward ~9, backward ~25).
-OPS_PER_EVAL = {"render_fwd": 9, "render_bwd": 25}
-SM_FP32_LANES = 128
 
 
 def parse_args():
@@ -73,12 +71,19 @@ def parse_args():
                          "reference layer's base GEMM + row-chunked delta GEMMs (reference); every layer rendering "
                          "itself through the drop-in runtime, the reference's call pattern (dropin)")
     ap.add_argument("--batch", type=int, default=4, help="cfg4: samples per GPU")
-    ap.add_argument("--bwd-exp", choices=["expf", "ex2"], default="expf",
-                    help="backward basis: CUDA expf (default) or the base-2 hardware approximation "
-                         "(GF_CFG_BWD_EXP2; the forward's delta is bit-exact either way)")
-    ap.add_argument("--fwd-exp", choices=["expf", "ex2"], default="expf",
-                    help="bf16 forward basis: CUDA expf (default: RNE of the reference's fp32 sum) or the base-2 "
-                         "hardware approximation (GF_CFG_FWD_EXP2, within the bf16 tolerance)")
+    ap.add_argument("--bwd-exp", choices=["expf", "ex2"], default="ex2",
+                    help="backward basis: the base-2 hardware approximation (GF_CFG_BWD_EXP2, default; held to the "
+                         "same gradient tolerance) or CUDA expf as the reference; the line reports both")
+    ap.add_argument("--fwd-exp", choices=["expf", "ex2"], default="ex2",
+                    help="bf16 forward basis: the base-2 hardware approximation (GF_CFG_FWD_EXP2, default; within the "
+                         "bf16 tolerance) or CUDA expf (the RNE cast of the reference's fp32 sum)")
+    ap.add_argument("--no-configs", action="store_true", help="skip the cfg1/cfg2 single-field lines and the "
+                    "reference-extension timings (N=1)")
+    ap.add_argument("--fields", type=int, default=128,
+                    help="cfg3 slice for profiling: this many of the 128 fields, spread over the UNet's widths")
+    ap.add_argument("--profile-case", action="store_true",
+                    help="only run warm-up + steps of the workload eagerly and exit (the command that the ncu "
+                         "summaries under profiles/ capture)")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
     return a
@@ -170,13 +175,16 @@ class UNetWorkload:
     """Fields of the whole UNet, partitioned; this rank's batch and buffers."""
 
     def __init__(self, rank: int, world: int, exchange: str = "auto", groups: int = 4, bwd_exp2: bool = False,
-                 fwd_exp2: bool = False):
+                 fwd_exp2: bool = False, num_fields: int = 128):
         from guass_b200 import synthetic
         from guass_b200.batched import FieldBatch, pack_fields
         from guass_b200.partition import PartitionedRenderer, field_costs
 
         self.rank, self.world = rank, world
         self.fields = synthetic.cfg3()
+        if num_fields < len(self.fields):
+            keep = sorted(interleaved_order(len(self.fields))[:max(1, num_fields)])
+            self.fields = [self.fields[i] for i in keep]
         shapes = [(f.out_features, f.in_features, f.k) for f in self.fields]
         self.numels = [f.numel for f in self.fields]
         self.total_elements = sum(self.numels)
@@ -368,7 +376,7 @@ def run_e2e(w: UNetWorkload, steps: int, warmup: int, world: int):
             for o, p in zip(h["out"], (mu, chol, amp)):
                 o.copy_(p.grad, non_blocking=True)
         if world > 1:
-            all_gather_slots(w.gathered, w.rank)
+            all_gather_slots(w.gathered, w.layout, w.rank)
 
     for _ in range(warmup):
         step()
@@ -470,32 +478,185 @@ def reference_arm(a, rank, world):
 
 
 # ---------------------------------------------------------------------------
-SFU_EX2_PER_CLK = 16  # per SM
+# Rooflines.  The render kernels are neither a contraction nor HBM-bound (2-4
+# bytes per element against ~14 evaluations of the basis per element); they
+# are bound by one of three SM resources, per evaluation:
+#   issue  -- warp-instruction issue, 4 warp instructions (128 thread
+#             instructions) per SM per clock
+#   fp32   -- the FP32 lanes, 128 lane-operations per SM per clock (a packed
+#             f32x2 instruction is two operations)
+#   sfu    -- MUFU (ex2), 16 per SM per clock
+# The per-evaluation counts come from ncu instruction counters of the same
+# kernel (profiles/<kernel>.json); achieved = count x evaluations / CUDA-event
+# time of the launch, peak = SMs x rate x the SM clock sampled during the run.
+PIPE_RATE = {"issue": 128, "fp32": 128, "sfu": 16}
+PIPE_KEY = {"issue": "thread_inst", "fp32": "fp32_lane_ops", "sfu": "xu_thread_inst"}
 
 
-def step_roofline(evals_total, bytes_step, ms, sm_count, f_mhz, hbm_peak, world):
-    """Whole-step bound: t_bound = max(bytes / HBM, 2E / SFU, FP32 ops / FP32)
-    over the job's GPUs, E the exact (element, Gaussian) evaluations (one
-    exp each in the forward and the backward), FP32 ops = E x (9 + 25)."""
+def load_counters(name: str):
+    p = ROOT / "profiles" / f"{name}.json"
+    if not p.exists():
+        return None
+    try:
+        return json.loads(p.read_text())
+    except ValueError:
+        return None
+
+
+def kernel_name(kind: str, ex2: bool) -> str:
+    return f"{kind}32_{'ex2' if ex2 else 'expf'}"
+
+
+def pipe_roofline(name: str, evals: float, elements: float, ms: float, f_mhz: float, sm_count: int):
+    prof = load_counters(name)
+    if prof is None or ms <= 0:
+        return None
+    pipes = {}
+    for pipe, rate in PIPE_RATE.items():
+        per = float(prof["per_eval"][PIPE_KEY[pipe]])
+        achieved = per * evals / (ms / 1e3) / 1e12
+        peak = sm_count * rate * f_mhz * 1e6 / 1e12
+        pipes[pipe] = {"ops_per_eval": per, "achieved": achieved, "peak": peak, "frac": achieved / peak}
+    bound = max(pipes, key=lambda k: pipes[k]["frac"])
+    per_el = prof.get("dram_bytes_per_element")
+    return {"kernel": name, "bound": bound, "achieved": pipes[bound]["achieved"], "peak": pipes[bound]["peak"],
+            "unit": "Tops/s", "frac": pipes[bound]["frac"],
+            "traffic": per_el * elements if per_el is not None else None,
+            "pipes": pipes, "counters": f"profiles/{name}.json",
+            "definition": f"per-evaluation counts from ncu counters x {int(evals)} evaluations / CUDA-event launch "
+                          f"time; peaks = {sm_count} SMs x (issue 128, fp32 128, sfu 16) per clock x {f_mhz:.0f} MHz "
+                          "(sampled); bound = the resource with the largest fraction; traffic = ncu DRAM bytes "
+                          "per delta element x elements"}
+
+
+def step_roofline(evals_total, bytes_step, ms, sm_count, f_mhz, hbm_peak, world, fwd_name, bwd_name):
+    """Whole-step bound: t_bound = sum over the two render kernels of their
+    binding resource's time at peak (counter-derived), against HBM bytes / BW."""
     clk = f_mhz * 1e6
-    terms = {"hbm_ms": bytes_step / (hbm_peak * 1e9 * world) * 1e3,
-             "sfu_ms": 2 * evals_total / (sm_count * SFU_EX2_PER_CLK * clk * world) * 1e3,
-             "fp32_ms": evals_total * sum(OPS_PER_EVAL.values()) / (sm_count * SM_FP32_LANES * clk * world) * 1e3}
-    bound = max(terms, key=terms.get)
-    return {"t_bound_ms": terms[bound], "binding": bound[:-3], "t_measured_ms": ms, "frac": terms[bound] / ms,
-            "terms": terms, "clock_mhz": f_mhz,
-            "definition": "t_bound / t_measured; peaks: HBM = MEASURED_PEAKS.json hbm_gbs, SFU = SMs x 16 ex2/clk, "
-                          "FP32 = SMs x 128 lanes, at the sampled SM clock"}
-
-
-def load_traffic(kernel: str):
-    p = ROOT / "profiles" / f"{kernel}_unet_traffic.json"
-    if p.exists():
-        try:
-            return json.loads(p.read_text())
-        except ValueError:
+    terms = {"hbm_ms": bytes_step / (hbm_peak * 1e9 * world) * 1e3}
+    t_kernels = 0.0
+    for name in (fwd_name, bwd_name):
+        prof = load_counters(name)
+        if prof is None:
             return None
-    return None
+        t = max(float(prof["per_eval"][PIPE_KEY[p]]) * evals_total / (sm_count * r * clk * world)
+                for p, r in PIPE_RATE.items())
+        terms[name + "_ms"] = t * 1e3
+        t_kernels += t * 1e3
+    t_bound = max(terms["hbm_ms"], t_kernels)
+    return {"t_bound_ms": t_bound, "t_measured_ms": ms, "frac": t_bound / ms, "terms": terms, "clock_mhz": f_mhz,
+            "definition": "t_bound = max(HBM bytes / MEASURED_PEAKS hbm_gbs, sum over the forward and backward "
+                          "render of their binding resource at peak) / t_measured"}
+
+
+# ---------------------------------------------------------------------------
+def time_single_field(f, fwd_exp2: bool, bwd_exp2: bool, out_dtype, steps: int, warmup: int):
+    """One field (FieldBatch of 1): forward + backward per step, CUDA events."""
+    from guass_b200 import _lib
+    from guass_b200.batched import FieldBatch, pack_fields
+    from guass_b200.partition import field_costs
+
+    L = _lib.lib()
+    b = FieldBatch([(f.out_features, f.in_features, f.k)], out_dtype=out_dtype, fwd_exp2=fwd_exp2,
+                   bwd_exp2=bwd_exp2)
+    mu, chol, amp, grad = pack_fields([f], device="cuda")
+    while b.ensure_capacity(mu, chol, amp):
+        pass
+    evals = field_costs([b.tile_ptr_view(0).cpu()], [(f.out_features, f.in_features)])[0]
+
+    def step():
+        b.forward(mu, chol, amp)
+        b.backward(grad, mu, chol, amp)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(7 * steps)]
+    for e in evs:
+        e.record()
+    torch.cuda.synchronize()
+    handles = (ctypes.c_void_p * len(evs))(*[e.cuda_event for e in evs])
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _lib.check(L.gf_trace_events(handles, len(evs)))
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    _lib.check(L.gf_trace_events(None, 0))
+    assert b.device_flags() == 0
+    ms = start.elapsed_time(end) / steps
+    kern = {"render_fwd": 0.0, "render_bwd": 0.0}
+    for s_ in range(steps):
+        e = evs[7 * s_: 7 * s_ + 7]
+        kern["render_fwd"] += e[1].elapsed_time(e[2]) / steps
+        kern["render_bwd"] += e[4].elapsed_time(e[5]) / steps
+    return ms, kern, evals
+
+
+def time_reference_cuda(fields, out_bf16: bool, steps: int, warmup: int):
+    """The reference's own CUDA extension (built unmodified into oracle/_ref),
+    called per field as GaussianLinear does: forward (fp32 delta, + the layer's
+    bf16 cast where the config stores bf16), then the training backward.
+    CUDA events on the stream it uses (the current one); its host reads of
+    the pair count are part of its time.  None when the build is absent."""
+    try:
+        from oracle import build_ref
+        ext = build_ref.load()
+    except (FileNotFoundError, ImportError, OSError):
+        return None
+    dev = [f.to("cuda") for f in fields]
+
+    def step():
+        for d in dev:
+            delta, tp, ids = ext.gaussian_field_forward(d.row_coords, d.col_coords, d.mu, d.chol_raw, d.amp, 32, 32,
+                                                        3.0, False, 80.0)
+            if out_bf16:
+                delta.to(torch.bfloat16)
+            ext.gaussian_field_backward(d.grad, d.row_coords, d.col_coords, d.mu, d.chol_raw, d.amp, tp, ids, 32, 32,
+                                        3.0, False, 80.0)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / steps
+
+
+def single_field_configs(a, f_mhz, sm_count):
+    """BASELINE configs 1 and 2 at N=1: one field each, forward + backward."""
+    from guass_b200 import synthetic
+
+    out = {}
+    for name, f, out_dtype, dt in (("cfg1", synthetic.cfg1(), torch.bfloat16, "bf16"),
+                                   ("cfg2", synthetic.cfg2(), torch.float32, "f32")):
+        fx = a.fwd_exp == "ex2" and out_dtype == torch.bfloat16
+        bx = a.bwd_exp == "ex2"
+        steps = max(a.steps, 20)
+        ms, kern, evals = time_single_field(f, fx, bx, out_dtype, steps, a.warmup)
+        ms_ref_basis, _, _ = time_single_field(f, False, False, out_dtype, steps, a.warmup)
+        ref_ms = time_reference_cuda([f], out_dtype == torch.bfloat16, max(3, steps // 4), 2)
+        dom = max(kern, key=kern.get)
+        kind = "render_fwd" if dom == "render_fwd" else "render_bwd"
+        out[name] = {
+            "workload": f"{name}: {f.out_features}x{f.in_features} field, K={f.k}, {dt} delta, f32 dL/d(delta)",
+            "value": f.numel / (ms / 1e3), "unit": "elements/s", "ms_per_step": ms, "evals": evals,
+            "forward_basis": "ex2.approx" if fx else "expf", "backward_basis": "ex2.approx" if bx else "expf",
+            "kernels_ms": kern,
+            "roofline": pipe_roofline(kernel_name(kind, fx if kind == "render_fwd" else bx), evals, f.numel,
+                                      kern[dom], f_mhz, sm_count),
+            "reference_basis_ms_per_step": ms_ref_basis,
+            "ref_cuda": None if ref_ms is None else {
+                "ms_per_step": ref_ms, "value": f.numel / (ref_ms / 1e3), "speedup": ref_ms / ms,
+                "what": "reference extension (oracle/_ref, unmodified gaussian_peft/cuda_field/csrc) forward"
+                        + (" + bf16 cast" if out_dtype == torch.bfloat16 else "") + " + backward, same inputs"},
+        }
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -521,6 +682,7 @@ def train_arm(a, rank: int, world: int, local: int) -> None:
         bank = sd15.PerLayerRender(mods)
     else:
         bank = BatchedAdapters(mods, out_dtype=torch.bfloat16, fused_weight=(a.adapter_apply == "fused"),
+                               fast_exp=(a.fwd_exp == "ex2" and a.bwd_exp == "ex2"),
                                track_metadata=False)  # no per-step diagnostic read-back in the timed loop
     bank.install()
     tr = sd15.DataParallelTrainer(model, bank, world=world)
@@ -561,6 +723,7 @@ def train_arm(a, rank: int, world: int, local: int) -> None:
     barrier(world)
     torch.cuda.synchronize()
     _lib.check(L.gf_trace_events(handles, len(evs)))
+    tr.allreduce_events = [] if world > 1 else None
     start.record()
     for _ in range(a.steps):
         loss = tr.step(inp)
@@ -590,6 +753,10 @@ def train_arm(a, rank: int, world: int, local: int) -> None:
         kern = {k: max_over_ranks(sum(v) / len(v), world) for k, v in per.items()}
     else:
         kern = {"unavailable": "a drop-in forward re-rendered for a larger id buffer inside the timed loop"}
+    if tr.allreduce_events:
+        kern["allreduce"] = max_over_ranks(sum(x.elapsed_time(y) for x, y in tr.allreduce_events)
+                                           / len(tr.allreduce_events), world)
+    tr.allreduce_events = None
     clocks = sampler.stop() if sampler else None
     assert torch.isfinite(loss).item()
 
@@ -619,14 +786,13 @@ def train_arm(a, rank: int, world: int, local: int) -> None:
     if rank == 0:
         sm_count = torch.cuda.get_device_properties(0).multi_processor_count
         f_mhz = (clocks or {}).get("sm_mhz") or 1965.0
-        peak = sm_count * SM_FP32_LANES * f_mhz * 1e6 / 1e12
+        fast = a.adapter_apply != "dropin" and a.fwd_exp == "ex2" and a.bwd_exp == "ex2"
         roofline = None
         if "render_bwd" in kern:
-            achieved = evals * OPS_PER_EVAL["render_bwd"] / (kern["render_bwd"] / 1e3) / 1e12
-            roofline = {"kernel": "render_bwd", "bound": "fp32", "achieved": achieved, "peak": peak,
-                        "unit": "Tops/s", "frac": achieved / peak, "traffic": None,
-                        "definition": "as the cfg3 line: 25 FMA-pipe ops per evaluation / CUDA-event launch time"
-                                      + (" (summed over the per-layer launches)" if calls > 1 else "")}
+            roofline = pipe_roofline(kernel_name("render_bwd", fast), evals, elements, kern["render_bwd"], f_mhz,
+                                     sm_count)
+            if roofline is not None and calls > 1:
+                roofline["definition"] += " (summed over the per-layer launches)"
         samples = a.batch * world
         line = {
             "metric": TRAIN_METRIC, "value": samples / (ms / 1e3), "unit": "samples/s", "n_gpus": world,
@@ -637,6 +803,7 @@ def train_arm(a, rank: int, world: int, local: int) -> None:
                        "latent": [cfg.latent_channels, cfg.latent_size, cfg.latent_size],
                        "text": [cfg.text_tokens, cfg.cross_dim], "adapters": nf, "K": cfg.num_gaussians,
                        "delta_elements": elements, "evals": evals, "adapter_apply": a.adapter_apply,
+                       "render_bases": "ex2.approx (forward and backward)" if fast else "expf",
                        "parallelism": f"dp{world}: flat NCCL all-reduce of Gaussian-parameter gradients"
                        if world > 1 else "single GPU", "optimizer": "AdamW on mu_raw/chol_raw/amp",
                        "l2": "no flush: the UNet step streams GBs of activations and weights"},
@@ -672,28 +839,49 @@ def main():
         reference_arm(a, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))
         return
     rank, world, local = setup_dist()
-    w = UNetWorkload(rank, world, a.exchange, a.groups, bwd_exp2=(a.bwd_exp == "ex2"), fwd_exp2=(a.fwd_exp == "ex2"))
+    fx, bx = a.fwd_exp == "ex2", a.bwd_exp == "ex2"
+    w = UNetWorkload(rank, world, a.exchange, a.groups, bwd_exp2=bx, fwd_exp2=fx, num_fields=a.fields)
+    if a.profile_case:
+        for _ in range(a.warmup + a.steps):
+            w.step()
+        torch.cuda.synchronize()
+        if rank == 0:
+            print(f"profile case: {len(w.fields)} fields, {w.total_elements} elements, {w.total_evals} evaluations, "
+                  f"{a.warmup + a.steps} steps", flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     sampler = ClockSampler() if local == 0 else None
     if sampler:
         sampler.start()
         time.sleep(0.3)
         sampler.mark("t0")
-    if world == 1 or w.renderer.symm is not None:
-        # CUDA-graph replays (no NCCL inside the graph)
-        _, kern = run_device_timed(w, max(3, min(a.steps, 10)), a.warmup, world)
-        ms_local = run_graph_timed(w, a.steps, a.warmup, world)
-        timing = "value: CUDA-graph replays of the whole step; kernels_ms: eager steps with per-launch trace events"
-    else:
-        # NCCL collectives are never captured into a graph (a captured all-gather
-        # hung process teardown on this system); the step runs eagerly
-        ms_local, kern = run_device_timed(w, a.steps, a.warmup, world)
-        timing = "value and kernels_ms: eager steps (NCCL exchange) with per-launch trace events"
+    # The same timing at every N: eager steps (a few dozen launches on two
+    # streams), CUDA events, max over ranks.  NCCL collectives are never
+    # captured into a graph (a captured all-gather hung process teardown on
+    # this system); at N=1 a CUDA-graph replay is reported beside it.
+    ms_local, kern = run_device_timed(w, a.steps, a.warmup, world)
     if sampler:
         sampler.mark("t1")
     ms = max_over_ranks(ms_local, world)
     kern_max = {k: max_over_ranks(v, world) for k, v in kern.items()}
     clocks = sampler.stop() if sampler else None
     value = w.total_elements / (ms / 1e3)
+    graph_ms = None
+    if world == 1 or w.renderer.symm is not None:
+        graph_ms = max_over_ranks(run_graph_timed(w, a.steps, a.warmup, world), world)
+
+    # the reference's arithmetic (expf in both passes) on the same workload
+    ref_basis = None
+    if fx or bx:
+        for b in w.renderer.batches:
+            b.set_bases(fwd_exp2=False, bwd_exp2=False)
+        ms_e, kern_e = run_device_timed(w, max(3, a.steps // 2), a.warmup, world)
+        ref_basis = {"ms_per_step": max_over_ranks(ms_e, world),
+                     "kernels_ms": {k: max_over_ranks(v, world) for k, v in kern_e.items()}}
+        ref_basis["value"] = w.total_elements / (ref_basis["ms_per_step"] / 1e3)
+        for b in w.renderer.batches:
+            b.set_bases(fwd_exp2=fx, bwd_exp2=bx)
 
     e2e = e2e_layer = None
     if not a.no_e2e:
@@ -717,23 +905,39 @@ def main():
         except Exception as exc:
             e2e_layer = {"error": f"{type(exc).__name__}: {exc}"}
 
+    sm_count = torch.cuda.get_device_properties(0).multi_processor_count
+    f_mhz = (clocks or {}).get("sm_mhz") or 1965.0
+    extra = {}
     cpu = None
-    if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        cpu = cpu_baseline(w.fields, a.cpu_seconds)
+    if rank == 0 and world == 1:
+        if not a.no_configs:
+            try:
+                extra["configs"] = single_field_configs(a, f_mhz, sm_count)
+            except Exception as exc:  # noqa: BLE001
+                extra["configs"] = {"error": f"{type(exc).__name__}: {exc}"}
+            ref_ms = time_reference_cuda(w.fields, True, 2, 1)
+            if ref_ms is not None:
+                extra["ref_cuda"] = {"ms_per_step": ref_ms, "value": w.total_elements / (ref_ms / 1e3),
+                                     "speedup": ref_ms / ms,
+                                     "what": "reference extension (oracle/_ref, unmodified gaussian_peft/cuda_field/"
+                                             "csrc), per layer as GaussianLinear calls it: forward + bf16 cast + "
+                                             "backward for each of the fields, same inputs, CUDA events"}
+        if not a.no_cpu_baseline:
+            cpu = cpu_baseline(w.fields, a.cpu_seconds)
 
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
         return
-    # roofline of the dominant kernel (render_bwd): FMA-pipe ops per launch
-    sm_count = torch.cuda.get_device_properties(0).multi_processor_count
-    f_mhz = (clocks or {}).get("sm_mhz") or 1965.0
+    # the slowest rank's launch processes its share of the evaluations
+    evals = w.total_evals if world == 1 else max(sum(w.costs[i] for i in p) for p in w.parts)
+    elements = w.total_elements if world == 1 else max(sum(w.fields[i].numel for i in p) for p in w.parts)
     dom = max(("render_fwd", "render_bwd"), key=lambda k: kern_max[k])
-    evals = w.total_evals if world == 1 else max(
-        sum(w.costs[i] for i in p) for p in w.parts)  # the slowest rank's launch
-    achieved = evals * OPS_PER_EVAL[dom] / (kern_max[dom] / 1e3) / 1e12
-    peak = sm_count * SM_FP32_LANES * f_mhz * 1e6 / 1e12
-    traffic = load_traffic(dom)
+    roofline = pipe_roofline(kernel_name(dom, fx if dom == "render_fwd" else bx), evals, elements, kern_max[dom],
+                             f_mhz, sm_count)
+    other = "render_fwd" if dom == "render_bwd" else "render_bwd"
+    roofline_other = pipe_roofline(kernel_name(other, fx if other == "render_fwd" else bx), evals, elements,
+                                   kern_max[other], f_mhz, sm_count)
     bytes_step = w.total_elements * (2 + 4)  # bf16 delta written + fp32 dL/d(delta) read
     with open(ROOT / "MEASURED_PEAKS.json") if (ROOT / "MEASURED_PEAKS.json").exists() else open(os.devnull) as fh:
         txt = fh.read()
@@ -742,32 +946,31 @@ def main():
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded; BASELINE cfg3 shapes and cfg1 distributions)",
-        "config": {"workload": "cfg3 whole-UNet batched render, 128 projection fields, K=256",
+        "config": {"workload": f"cfg3 whole-UNet batched render, {len(w.fields)} projection fields, K=256",
                    "elements": w.total_elements, "pairs": w.total_pairs, "evals": w.total_evals,
                    "delta_dtype": "bf16", "grad_dtype": "f32", "tile": "32x32", "sigma_multiplier": 3.0,
-                   "backward_basis": "ex2.approx" if a.bwd_exp == "ex2" else "expf",
-                   "forward_basis": "ex2.approx" if a.fwd_exp == "ex2" else "expf",
+                   "forward_basis": "ex2.approx" if fx else "expf",
+                   "backward_basis": "ex2.approx" if bx else "expf",
                    "clamp_quad": 80.0, "partition": f"LPT by render cost over {world} rank(s)",
                    "parallelism": f"layer-partition x{world} + {w.renderer.exchange} of bf16 delta "
-                                  f"({len(w.renderer.batches)} field groups)" if world > 1 else "single GPU",
+                                  f"({w.layout.num_groups} field groups)" if world > 1 else "single GPU",
                    "l2": "no flush: each step writes 187 MB of delta and reads 374 MB of dL/d(delta) (> 126 MB L2)"},
         "kernels_ms": kern_max,
-        "timing": timing,
-        "roofline": {"kernel": dom, "bound": "fp32", "achieved": achieved, "peak": peak, "unit": "Tops/s",
-                     "frac": achieved / peak,
-                     "traffic": (traffic or {}).get("bytes_per_launch"),
-                     "definition": f"{OPS_PER_EVAL[dom]} FMA-pipe ops x {evals} (element,Gaussian) evaluations "
-                                   f"per launch / CUDA-event launch time; peak = {sm_count} SMs x "
-                                   f"{SM_FP32_LANES} FP32 lanes x {f_mhz:.0f} MHz (sampled SM clock; "
-                                   "MEASURED_PEAKS.json has no FP32 figure)"},
-        "roofline_step": step_roofline(evals_total=w.total_evals, bytes_step=bytes_step, ms=ms, sm_count=sm_count,
-                                       f_mhz=f_mhz, hbm_peak=hbm_peak, world=world),
+        "timing": "value and kernels_ms: eager steps with per-launch trace events (every N); graph_ms_per_step: "
+                  "the same step replayed as one CUDA graph",
+        "graph_ms_per_step": graph_ms,
+        "roofline": roofline,
+        "roofline_other_kernel": roofline_other,
+        "roofline_step": step_roofline(w.total_evals, bytes_step, ms, sm_count, f_mhz, hbm_peak, world,
+                                       kernel_name("render_fwd", fx), kernel_name("render_bwd", bx)),
         "roofline_hbm": {"achieved": bytes_step / (ms / 1e3) / 1e9, "peak": hbm_peak, "unit": "GB/s",
                          "frac": bytes_step / (ms / 1e3) / 1e9 / hbm_peak, "peak_source": "MEASURED_PEAKS.json hbm_gbs"},
+        "reference_basis": ref_basis,
         "clocks": clocks,
         "e2e": e2e,
         "e2e_dropin_per_layer": e2e_layer,
         "cpu_baseline": cpu,
+        **extra,
         # per field group: bin, render, prep, backward render, finalize (+ the publish kernel of the
         # multicast exchange; the fused exchange stores from the render itself)
         "gpu_launches": (5 * len(w.renderer.batches)

@@ -97,7 +97,7 @@ class BatchedAdapters:
     """
 
     def __init__(self, modules: dict, batch_factory=None, out_dtype=torch.bfloat16, fused_weight: bool = False,
-                 track_metadata: bool = True):
+                 track_metadata: bool = True, fast_exp: bool = False):
         self.names = list(modules)
         self.modules = [modules[n] for n in self.names]
         if not self.modules:
@@ -112,6 +112,11 @@ class BatchedAdapters:
         kw = dict(tile_out=cfg.tile_out, tile_in=cfg.tile_in, sigma_multiplier=cfg.sigma_multiplier,
                   normalize=cfg.normalize_gaussian, clamp_quad=80.0,  # gaussian_linear.py:189
                   out_dtype=out_dtype, grad_dtype=out_dtype)
+        # fast_exp: both passes on the base-2 hardware exponential (GF_CFG_FWD_EXP2 for bf16
+        # deltas, GF_CFG_BWD_EXP2); tolerance-bound instead of the reference's expf
+        self.fast_exp = bool(fast_exp)
+        if self.fast_exp:
+            kw.update(fwd_exp2=True, bwd_exp2=True)
         self.fused = bool(fused_weight)
         self.track_metadata = bool(track_metadata)
         self.w0 = None
@@ -171,7 +176,7 @@ class BatchedAdapters:
         """A new binding for the modules' current K (keeps install state)."""
         fresh = BatchedAdapters(dict(zip(self.names, self.modules)), batch_factory=self._factory,
                                 out_dtype=self._out_dtype, fused_weight=self.fused,
-                                track_metadata=self.track_metadata)
+                                track_metadata=self.track_metadata, fast_exp=self.fast_exp)
         if self._orig:
             self.uninstall()
             fresh.install()

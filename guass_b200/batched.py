@@ -119,6 +119,16 @@ class FieldBatch:
         for f in range(len(self.shapes)):
             self._fields[f].delta_multicast = None if not address else int(address) + esz * self.n_off[f]
 
+    def set_bases(self, *, fwd_exp2: bool | None = None, bwd_exp2: bool | None = None) -> None:
+        """Switch the exponential of later calls: the base-2 hardware
+        approximation (GF_CFG_FWD_EXP2 for a bf16 forward, GF_CFG_BWD_EXP2 for
+        the backward) or the reference's expf (False).  None keeps the current."""
+        flags = int(self.cfg.flags)
+        for bit, on in ((_lib.GF_CFG_FWD_EXP2, fwd_exp2), (_lib.GF_CFG_BWD_EXP2, bwd_exp2)):
+            if on is not None:
+                flags = (flags | bit) if on else (flags & ~bit)
+        self.cfg.flags = flags
+
     def set_base_weight(self, base_weight: torch.Tensor | None) -> None:
         """Fused weight: later forwards store ``W0 + out_scale * value`` (one
         rounding to out_dtype) with W0 = ``base_weight`` (packed like delta;

@@ -76,7 +76,7 @@ struct DevField {
   int32_t g_base;     // first global Gaussian index
   int32_t diff_base;  // first int of this field's global diff array
   int32_t vec_ok;     // delta (and base) rows are 16-byte aligned for vector access
-  int32_t pad_;
+  int32_t gvec_ok;    // grad rows are 16-byte aligned for vector access
 };
 
 template <int NF>
@@ -633,6 +633,15 @@ __device__ __forceinline__ f2 sub2(f2 a, f2 b) {
   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+// 2^x of both halves; one asm block so that the result stays in the input's
+// register pair (no moves to re-pack the two MUFU results)
+__device__ __forceinline__ f2 ex2_2(f2 x) {
+  f2 r;
+  asm("{\n\t.reg .f32 a, b;\n\tmov.b64 {a, b}, %1;\n\tex2.approx.ftz.f32 a, a;\n\tex2.approx.ftz.f32 b, b;\n\t"
+      "mov.b64 %0, {a, b};\n\t}"
+      : "=l"(r) : "l"(x));
+  return r;
+}
 
 // ---------------------------------------------------------------------------
 // Forward kernel 2, 32x32-tile fast path: one CTA of kFwd32Warps warps per
@@ -649,12 +658,21 @@ __device__ __forceinline__ f2 sub2(f2 a, f2 b) {
 #define GF_FWD32_WARPS 2
 #endif
 constexpr int kFwd32Warps = GF_FWD32_WARPS;
+// the base-2 variant does less work per element, so each warp takes more rows
+// to amortise its per-Gaussian set-up
+#ifndef GF_FWD32_WARPS_EX2
+#define GF_FWD32_WARPS_EX2 1
+#endif
+constexpr int kFwd32WarpsEx2 = GF_FWD32_WARPS_EX2;
+template <bool EX2>
+__host__ __device__ constexpr int fwd32_warps() { return EX2 ? kFwd32WarpsEx2 : kFwd32Warps; }
 
 template <int NF, bool NORM, bool CLAMP, int OUTT, bool EX2>
-__global__ void __launch_bounds__(32 * kFwd32Warps)
+__global__ void __launch_bounds__(32 * fwd32_warps<EX2>())
 render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
-  constexpr int R = 32 / kFwd32Warps;  // rows per warp
-  __shared__ __align__(16) float s_out[kFwd32Warps][R][36];
+  constexpr int NW = fwd32_warps<EX2>();
+  constexpr int R = 32 / NW;  // rows per warp
+  __shared__ __align__(16) float s_out[NW][R][36];
   const int tg = blockIdx.x;
   const int fi = field_of_tile(p, tg);
   const DevField& F = p.f[fi];
@@ -705,7 +723,7 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
       if (pos < cap_left) ids[pos] = g;
     }
     found += __popc(m);
-    if (EX2) {
+    if constexpr (EX2) {
       // bf16 output (GF_CFG_FWD_EXP2): the form in base 2 with the column
       // terms hoisted, q2 = dx*(g00*dx + 2*g01*dy) + g11*dy^2 (g = log2e*h),
       // and the basis 2^q2 from MUFU.EX2; the normalisation folds into the
@@ -727,18 +745,16 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
 #pragma unroll
         for (int i = 0; i < R / 2; ++i) {
           const f2 DX = sub2(CR[i], MUR);
-          const f2 Q = fma2(DX, fma2(G00, DX, B1), C0);
-          float q0, q1;
-          up2(Q, q0, q1);
+          f2 Q = fma2(DX, fma2(G00, DX, B1), C0);
           if (CLAMP) {
-            q0 = fmaxf(q0, nclamp2);
-            q1 = fmaxf(q1, nclamp2);
+            float q0, q1;
+            up2(Q, q0, q1);
+            Q = pk2(fmaxf(q0, nclamp2), fmaxf(q1, nclamp2));
           }
-          V[i] = fma2(AMP, pk2(ex2_approx(q0), ex2_approx(q1)), V[i]);
+          V[i] = fma2(AMP, ex2_2(Q), V[i]);
         }
       }
-      continue;
-    }
+    } else {
     while (m) {
       const int gg = k0 + __ffs(m) - 1;
       m &= m - 1;
@@ -770,6 +786,7 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
         }
         V[i] = fma2(AMP, pk2(e0, e1), V[i]);
       }
+    }
     }
   }
   if (warp == 0 && lane == 0 && found != count) atomicOr(p.status, GF_FLAG_INTERNAL);
@@ -848,6 +865,14 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
   if (F.mc) __threadfence_system();
 }
 
+// Lower bound of the scaled form q' = -0.5*quad at one tile corner, minus
+// the evaluation-error margin (h* are the -0.5-scaled inverse entries).
+__device__ __forceinline__ float corner_bound(float dx, float dy, float h00, float h01, float h11) {
+  const float q = dx * (h00 * dx + h01 * dy) + dy * (h01 * dx + h11 * dy);
+  const float s = fabsf(h00) * dx * dx + 2.0f * fabsf(h01) * fabsf(dx * dy) + fabsf(h11) * dy * dy;
+  return q - 1e-5f * s;
+}
+
 // ---------------------------------------------------------------------------
 // Backward kernel 1: per-field preprocess (backward.cu:552-557 rebuilds the
 // geometry too), plus each Gaussian's first slot in the pair-partial buffer:
@@ -860,13 +885,48 @@ bwd_prep_kernel(const __grid_constant__ Params<NF> p) {
   const int fi = blockIdx.x;
   const DevField& F = p.f[fi];
   const int tid = threadIdx.x, bs = blockDim.x;
+  // Are the axes monotonic?  Then the coordinates of any range of rows (or
+  // columns) lie between the range's end values, which the clamp bounds use.
+  bool mono = true;
+  if (p.cfg.has_clamp) {
+    bool up_r = true, dn_r = true, up_c = true, dn_c = true;
+    for (int i = tid; i + 1 < F.out_f; i += bs) {
+      const float a = F.row[i], b = F.row[i + 1];
+      up_r &= a <= b; dn_r &= a >= b;
+    }
+    for (int i = tid; i + 1 < F.in_f; i += bs) {
+      const float a = F.col[i], b = F.col[i + 1];
+      up_c &= a <= b; dn_c &= a >= b;
+    }
+    const int ur = __syncthreads_and(up_r), dr = __syncthreads_and(dn_r);
+    const int uc = __syncthreads_and(up_c), dc = __syncthreads_and(dn_c);
+    mono = (ur || dr) && (uc || dc);
+  }
   const int per = (F.K + bs - 1) / bs;
   const int g0 = min(F.K, tid * per), g1 = min(F.K, g0 + per);
   int64_t local = 0;
   for (int g = g0; g < g1; ++g) {
     const float mu_r = F.mu[2 * g], mu_c = F.mu[2 * g + 1];
     const Geo geo = geometry(mu_r, mu_c, F.chol[3 * g], F.chol[3 * g + 1], F.chol[3 * g + 2], F, p.cfg);
-    store_record(p.records + 2 * (size_t)(F.g_base + g), mu_r, mu_c, F.amp[g], geo);
+    float4* rec = p.records + 2 * (size_t)(F.g_base + g);
+    store_record(rec, mu_r, mu_c, F.amp[g], geo);
+    if (p.cfg.has_clamp) {
+      // May any element of any of this Gaussian's tiles reach the clamp?  The
+      // form is convex, so over the rectangle of its tile-aligned box it is
+      // largest at a corner.  The answer travels as the sign of the record's
+      // (positive) normalisation factor: negative = test per tile.
+      bool may = true;
+      if (mono) {
+        const int ra = geo.box.x * p.cfg.tile_out, rb = min((geo.box.y + 1) * p.cfg.tile_out, F.out_f) - 1;
+        const int ca = geo.box.z * p.cfg.tile_in, cb = min((geo.box.w + 1) * p.cfg.tile_in, F.in_f) - 1;
+        const float h00 = -0.5f * geo.i00, h01 = -0.5f * geo.i01, h11 = -0.5f * geo.i11;
+        const float x0 = F.row[ra] - mu_r, x1 = F.row[rb] - mu_r, y0 = F.col[ca] - mu_c, y1 = F.col[cb] - mu_c;
+        const float lo = fminf(fminf(corner_bound(x0, y0, h00, h01, h11), corner_bound(x0, y1, h00, h01, h11)),
+                               fminf(corner_bound(x1, y0, h00, h01, h11), corner_bound(x1, y1, h00, h01, h11)));
+        may = !(lo > p.cfg.nclamp);
+      }
+      if (may) rec[0].w = -rec[0].w;
+    }
     p.boxes[F.g_base + g] = geo.box;
     local += (int64_t)(geo.box.y - geo.box.x + 1) * (geo.box.w - geo.box.z + 1);
   }
@@ -913,16 +973,17 @@ __device__ __forceinline__ float load_grad(const void* g, size_t i) {
 // per-element work is the basis plus six running sums (gba = g*b where the
 // q-gradient is active, 0 where the form is clamped):
 //   T0 = sum g*b,  U0 = sum gba,  U1 = sum gba*dx,  U2 = sum gba*dx^2,
-//   M0 = sum gba*(h00*dx + h01*dy),  M1 = sum gba*(h01*dx + h11*dy)
+//   M0 = sum gba*fma(h01, dy, h00*dx),  M1 = sum gba*fma(h11, dy, h01*dx)
 // (h = -0.5*A), from which the reference's per-pair channels follow
 // (backward.cu:330-351, with A01 == A10):
 //   amp: T0    mu0: -2*M0    mu1: -2*M1
 //   A00: U2    A01 = A10: dy*U1    A11: dy^2*U0      (times amp, -0.5 later)
-// The mu factors are evaluated per element with the reference's roundings:
-// for an elongated Gaussian A00*dx and A01*dy nearly cancel, and a sum
-// factored as A00*U1 + A01*dy*U0 would carry their rounding, not that of the
-// (much smaller) per-element terms.  The A factors carry no such cancellation
-// (dy is exact per lane), so they stay factored.
+// The mu factors are evaluated per element with the reference's roundings
+// (its build contracts dq/dmu0 = -(2*A00*dx + 2*A01*dy) to
+// -fma(2*A01, dy, 2*A00*dx)): for an elongated Gaussian A00*dx and A01*dy
+// nearly cancel, and a sum factored as A00*U1 + A01*dy*U0 would carry their
+// rounding, not that of the (much smaller) per-element terms.  The A factors
+// carry no such cancellation (dy is exact per lane), so they stay factored.
 // Lanes are reduced with a fixed xor-shuffle tree and lane 0 writes the six
 // channels to the pair's slot, goff[g] + (its tile's index in g's box), so the
 // finalize kernel reads each Gaussian's pairs contiguously.
@@ -1006,17 +1067,18 @@ render_bwd_kernel(const __grid_constant__ Params<NF> p) {
             q = fmaxf(q, nclamp);
           }
           float e = expf(q);
-          if (NORM) e = __fmul_rn(e, a.w);
+          if (NORM) e = __fmul_rn(e, fabsf(a.w));  // the sign carries a clamp flag
           const float gb = __fmul_rn(cval ? gcol[r * TI] : 0.0f, e);
           const float gba = act ? gb : 0.0f;
           blk[0] = __fadd_rn(blk[0], gb);
           blk[1] = __fadd_rn(blk[1], gba);
           blk[2] = __fmaf_rn(gba, dx, blk[2]);
           blk[3] = __fmaf_rn(__fmul_rn(gba, dx), dx, blk[3]);
-          // the reference's per-element mu factors (backward.cu:338-340),
-          // -0.25*dq/dmu with its roundings: h00*dx + h01*dy, h01*dx + h11*dy
-          blk[4] = __fmaf_rn(gba, __fadd_rn(__fmul_rn(h.x, dx), a01), blk[4]);
-          blk[5] = __fmaf_rn(gba, __fadd_rn(__fmul_rn(h.y, dx), a11), blk[5]);
+          // the reference's per-element mu factors (backward.cu:338-340) as
+          // its build rounds them, dq/dmu0 = -fma(2*A01, dy, 2*A00*dx), here
+          // scaled by -1/4 (exact): fma(h01, dy, h00*dx), fma(h11, dy, h01*dx)
+          blk[4] = __fmaf_rn(gba, __fmaf_rn(h.y, dy, __fmul_rn(h.x, dx)), blk[4]);
+          blk[5] = __fmaf_rn(gba, __fmaf_rn(h.z, dy, __fmul_rn(h.y, dx)), blk[5]);
         }
 #pragma unroll
         for (int k = 0; k < 6; ++k) acc[k] = __fadd_rn(acc[k], blk[k]);
@@ -1056,11 +1118,14 @@ render_bwd_kernel(const __grid_constant__ Params<NF> p) {
 //
 // Clamped elements (quad >= clamp_quad) lose their q-gradient
 // (backward.cu:318-321), which costs a max, a compare and a select per
-// element.  The quadratic form is convex, so over the tile it is largest at a
-// corner; when every corner is below the clamp by more than 1e-5 of the sum of
-// its absolute terms (about 20x the worst fp32 evaluation error of the element
-// formula), no element of the pair can be clamped and the loop without that
-// bookkeeping runs.  Results are identical either way.
+// element.  The quadratic form is convex, so over the rectangle spanned by the
+// tile's row and column coordinates (min to max, whatever their order) it is
+// largest at a corner; four lanes evaluate one corner each, and when every
+// corner is below the clamp by more than 1e-5 of the sum of its absolute terms
+// (about 20x the worst fp32 evaluation error of the element formula), no
+// element of the pair can be clamped and the loop without that bookkeeping
+// runs.  Results are identical either way.  The next pair's id, box and record
+// are loaded while the current pair computes.
 #ifndef GF_BWD32_WARPS
 #define GF_BWD32_WARPS 4
 #endif
@@ -1082,7 +1147,7 @@ __device__ __forceinline__ float exp_via_ex2(float q) { return ex2_approx(__fmul
 
 template <bool NORM, bool TRACK_CLAMP, bool EX2>
 __device__ __forceinline__ PairSums bwd32_pair_rows(const float* s_rows, const float* s_gcol, f2 H00, f2 H01,
-                                                   f2 A01, f2 A11, f2 DY, f2 MUR, float nclamp, float nf) {
+                                                   f2 H11, f2 A01, f2 A11, f2 DY, f2 MUR, float nclamp, float nf) {
   const f2 zero2 = pk2(0.0f, 0.0f);
   PairSums S{zero2, zero2, zero2, zero2, zero2, zero2};
 #pragma unroll
@@ -1093,9 +1158,16 @@ __device__ __forceinline__ PairSums bwd32_pair_rows(const float* s_rows, const f
     const f2 T2 = fma2(H01, DX, A11);
     const f2 Q = fma2(DX, T1, mul2(DY, T2));
     float q0, q1;
-    up2(Q, q0, q1);
-    q0 = fminf(q0, 0.0f);
-    q1 = fminf(q1, 0.0f);
+    f2 E2 = 0;
+    if (EX2 && !TRACK_CLAMP) {
+      // base-2 basis: one packed scaling; the max(quad, 0) of the reference
+      // only removes rounding noise of order 1e-7 here (2^q = 1 + O(q))
+      E2 = ex2_2(mul2(Q, pk2(kLog2e, kLog2e)));
+    } else {
+      up2(Q, q0, q1);
+      q0 = fminf(q0, 0.0f);
+      q1 = fminf(q1, 0.0f);
+    }
     bool act0 = true, act1 = true;
     if (TRACK_CLAMP) {
       act0 = q0 > nclamp;  // reference: quad < clamp
@@ -1103,20 +1175,20 @@ __device__ __forceinline__ PairSums bwd32_pair_rows(const float* s_rows, const f
       q0 = fmaxf(q0, nclamp);
       q1 = fmaxf(q1, nclamp);
     }
-    float e0, e1;
-    if (EX2) {
-      e0 = exp_via_ex2(q0);
-      e1 = exp_via_ex2(q1);
-    } else {
-      e0 = expf(q0);
-      e1 = expf(q1);
+    if (!(EX2 && !TRACK_CLAMP)) {
+      float e0, e1;
+      if (EX2) {
+        e0 = exp_via_ex2(q0);
+        e1 = exp_via_ex2(q1);
+      } else {
+        e0 = expf(q0);
+        e1 = expf(q1);
+      }
+      E2 = pk2(e0, e1);
     }
-    if (NORM) {
-      e0 = __fmul_rn(e0, nf);
-      e1 = __fmul_rn(e1, nf);
-    }
+    if (NORM) E2 = mul2(E2, pk2(nf, nf));
     const float2 gg = *reinterpret_cast<const float2*>(&s_gcol[2 * k]);
-    const f2 GB = mul2(pk2(gg.x, gg.y), pk2(e0, e1));
+    const f2 GB = mul2(pk2(gg.x, gg.y), E2);
     if (TRACK_CLAMP) S.T0 = add2(S.T0, GB);  // without clamped elements T0 == U0 (same terms, same order)
     f2 GBA = GB;
     if (TRACK_CLAMP) {
@@ -1128,19 +1200,11 @@ __device__ __forceinline__ PairSums bwd32_pair_rows(const float* s_rows, const f
     S.U1 = fma2(GBA, DX, S.U1);
     S.U2 = fma2(mul2(GBA, DX), DX, S.U2);
     // per-element mu factors with the reference's roundings (see render_bwd_kernel)
-    S.M0 = fma2(GBA, add2(mul2(H00, DX), A01), S.M0);
-    S.M1 = fma2(GBA, add2(mul2(H01, DX), A11), S.M1);
+    S.M0 = fma2(GBA, fma2(H01, DY, mul2(H00, DX)), S.M0);
+    S.M1 = fma2(GBA, fma2(H11, DY, mul2(H01, DX)), S.M1);
   }
   if (!TRACK_CLAMP) S.T0 = S.U0;
   return S;
-}
-
-// Lower bound of the scaled form q' = -0.5*quad at one tile corner, minus
-// the evaluation-error margin (h* are the -0.5-scaled inverse entries).
-__device__ __forceinline__ float corner_bound(float dx, float dy, float h00, float h01, float h11) {
-  const float q = dx * (h00 * dx + h01 * dy) + dy * (h01 * dx + h11 * dy);
-  const float s = fabsf(h00) * dx * dx + 2.0f * fabsf(h01) * fabsf(dx * dy) + fabsf(h11) * dy * dy;
-  return q - 1e-5f * s;
 }
 
 template <int NF, bool NORM, bool CLAMP, int GT, bool EX2>
@@ -1154,72 +1218,125 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
   const int t = tg - F.tile_base;
   const int tr = t / F.ntc, tc = t % F.ntc;
   const int64_t start = F.tile_ptr[t];
-  const int64_t count = F.tile_ptr[t + 1] - start;
-  if (count <= 0) return;
+  const int64_t count64 = F.tile_ptr[t + 1] - start;
+  if (count64 <= 0) return;
   const int64_t id_base = (p.batch_ids != nullptr) ? p.pair_base[fi] : 0;
   const int64_t id_limit = (p.batch_ids != nullptr) ? p.batch_cap : F.ids_cap;
-  if (start < 0 || id_base < 0 || id_base + start + count > id_limit) {
+  // a tile holds at most K pairs (one per Gaussian), K < 2^30
+  if (start < 0 || id_base < 0 || id_base + start + count64 > id_limit || count64 > F.K) {
     if (threadIdx.x == 0) atomicOr(p.status, GF_FLAG_STATE);
     return;
   }
+  const int count = (int)count64;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int row0 = tr * 32, col0 = tc * 32;
   const int th = min(32, F.out_f - row0), tw = min(32, F.in_f - col0);
   if (threadIdx.x < 32) s_rows[threadIdx.x] = (threadIdx.x < th) ? F.row[row0 + threadIdx.x] : 0.0f;
-  for (int e = threadIdx.x; e < 1024; e += blockDim.x) {
-    const int r = e >> 5, c = e & 31;
-    s_gt[c * 34 + r] =
-        (r < th && c < tw && GF_IN_BOUNDS((size_t)(row0 + r) * F.in_f + col0 + c < (size_t)F.out_f * F.in_f))
-            ? load_grad<GT>(F.grad, (size_t)(row0 + r) * F.in_f + col0 + c)
-            : 0.0f;
+  // dL/d(delta) of the tile, transposed into s_gt[col][row]
+  const size_t gbase = (size_t)row0 * F.in_f + col0;
+  if (th == 32 && tw == 32 && F.gvec_ok &&
+      GF_IN_BOUNDS(gbase + (size_t)31 * F.in_f + 31 < (size_t)F.out_f * F.in_f)) {
+    if (GT == GF_F32) {
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {  // 256 16-byte loads of 4 floats
+        const int q = threadIdx.x + k * (32 * kBwd32Warps);
+        if (q < 256) {
+          const int r = q >> 3, c = (q & 7) * 4;
+          const float4 v = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(F.grad) + gbase +
+                                                            (size_t)r * F.in_f + c);
+          s_gt[(c + 0) * 34 + r] = v.x;
+          s_gt[(c + 1) * 34 + r] = v.y;
+          s_gt[(c + 2) * 34 + r] = v.z;
+          s_gt[(c + 3) * 34 + r] = v.w;
+        }
+      }
+    } else {
+      const int q = threadIdx.x;  // 128 16-byte loads of 8 bf16
+      if (q < 128) {
+        const int r = q >> 2, c = (q & 3) * 8;
+        const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(F.grad) + gbase +
+                                                        (size_t)r * F.in_f + c);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
+          s_gt[(c + 2 * k) * 34 + r] = f.x;
+          s_gt[(c + 2 * k + 1) * 34 + r] = f.y;
+        }
+      }
+    }
+  } else {
+    for (int e = threadIdx.x; e < 1024; e += blockDim.x) {
+      const int r = e >> 5, c = e & 31;
+      s_gt[c * 34 + r] =
+          (r < th && c < tw && GF_IN_BOUNDS((size_t)(row0 + r) * F.in_f + col0 + c < (size_t)F.out_f * F.in_f))
+              ? load_grad<GT>(F.grad, (size_t)(row0 + r) * F.in_f + col0 + c)
+              : 0.0f;
+    }
   }
   __syncthreads();
   if (warp >= count) return;
   const bool cval = lane < tw;
   const float cc = cval ? F.col[col0 + lane] : 0.0f;
-  const float c_first = F.col[col0], c_last = F.col[col0 + tw - 1];
-  const float r_first = s_rows[0], r_last = s_rows[th - 1];
+  // Per-tile clamp test for Gaussians flagged by bwd_prep (record norm < 0):
+  // lanes 0..3 each evaluate one corner of the tile's coordinate rectangle
+  // (the flag is only clear when the axes are monotonic, so the rectangle is
+  // spanned by the first and last row and column; otherwise flagged
+  // Gaussians always take the clamp bookkeeping).
+  const float corner_r = s_rows[(lane & 1) ? th - 1 : 0];
+  const float corner_c = F.col[col0 + ((lane & 2) ? tw - 1 : 0)];
   const float* s_gcol = &s_gt[lane * 34];
   const int64_t* ids = ((p.batch_ids != nullptr) ? p.batch_ids : F.ids) + id_base + start;
   const float4* rec = p.records + 2 * (size_t)F.g_base;
   const int4* box = p.boxes + F.g_base;
+  const int64_t* goff = p.goff + F.g_base;
   const float nclamp = p.cfg.nclamp;
   // channel held by this lane after the reduce-scatter: bits 4,3,2 of lane
   const int my_ch = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
 
-  int64_t gid = ids[warp];
-  for (int64_t i = warp; i < count; i += kBwd32Warps) {
-    const int64_t cur = gid;
-    const int64_t prev = (i > 0) ? ids[i - 1] : -1;
-    if (i + kBwd32Warps < count) gid = ids[i + kBwd32Warps];
-    bool ok = (cur >= 0) && (cur < F.K) && (prev < cur);
-    int4 b = make_int4(0, -1, 0, -1);
-    if (ok) {
-      b = box[cur];
-      ok = (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
+  // software pipeline: the next pair's id, box and record load while this one computes
+  int gid = (int)ids[warp];
+  bool okn = (ids[warp] >= 0) && (ids[warp] < F.K) && (warp == 0 || ids[warp - 1] < ids[warp]);
+  int4 bn = okn ? box[gid] : make_int4(0, -1, 0, -1);
+  float4 an = okn ? rec[2 * gid] : make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 hn = okn ? rec[2 * gid + 1] : make_float4(0.f, 0.f, 0.f, 0.f);
+  int64_t gon = okn ? goff[gid] : -1;
+  for (int i = warp; i < count; i += kBwd32Warps) {
+    const int4 b = bn;
+    const float4 a = an, h = hn;
+    const int64_t go = gon;
+    const bool ok = okn && (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
+    const int inext = i + kBwd32Warps;
+    if (inext < count) {
+      const int64_t idn = ids[inext], idp = ids[inext - 1];
+      okn = (idn >= 0) && (idn < F.K) && (idp < idn);
+      gid = (int)idn;
+      if (okn) {
+        bn = box[gid];
+        an = rec[2 * gid];
+        hn = rec[2 * gid + 1];
+        gon = goff[gid];
+      }
     }
     if (!ok) {
       if (lane == 0) atomicOr(p.status, GF_FLAG_STATE);
       continue;
     }
-    const float4 a = rec[2 * cur];
-    const float4 h = rec[2 * cur + 1];
     const float dy = cval ? __fsub_rn(cc, a.y) : 0.0f;
     const float a01 = __fmul_rn(h.y, dy);
     const float a11 = __fmul_rn(h.z, dy);
     const f2 H00 = pk2(h.x, h.x), H01 = pk2(h.y, h.y), A01 = pk2(a01, a01), A11 = pk2(a11, a11);
     const f2 DY = pk2(dy, dy), MUR = pk2(a.x, a.x);
-    bool track = CLAMP;
-    if (CLAMP) {
-      // warp-uniform: every lane evaluates the same four corners
-      const float dx0 = r_first - a.x, dx1 = r_last - a.x;
-      const float dy0 = c_first - a.y, dy1 = c_last - a.y;
-      const float lo = fminf(fminf(corner_bound(dx0, dy0, h.x, h.y, h.z), corner_bound(dx0, dy1, h.x, h.y, h.z)),
-                             fminf(corner_bound(dx1, dy0, h.x, h.y, h.z), corner_bound(dx1, dy1, h.x, h.y, h.z)));
-      track = !(lo > nclamp);
+    bool track = false;
+    if (CLAMP && a.w < 0.0f) {  // flagged by bwd_prep: test this tile's corners (warp-uniform)
+      const bool far = corner_bound(corner_r - a.x, corner_c - a.y, h.x, h.y, h.z) > nclamp;
+      track = !__all_sync(0xffffffffu, far || lane >= 4);
     }
-    PairSums S = track ? bwd32_pair_rows<NORM, true, EX2>(s_rows, s_gcol, H00, H01, A01, A11, DY, MUR, nclamp, a.w)
-                       : bwd32_pair_rows<NORM, false, EX2>(s_rows, s_gcol, H00, H01, A01, A11, DY, MUR, nclamp, a.w);
+    const f2 H11 = pk2(h.z, h.z);
+    const float nf = fabsf(a.w);
+    PairSums S = track
+                     ? bwd32_pair_rows<NORM, true, EX2>(s_rows, s_gcol, H00, H01, H11, A01, A11, DY, MUR, nclamp, nf)
+                     : bwd32_pair_rows<NORM, false, EX2>(s_rows, s_gcol, H00, H01, H11, A01, A11, DY, MUR, nclamp, nf);
     float t0a, t0b, u0a, u0b, u1a, u1b, u2a, u2b, m0a, m0b, m1a, m1b;
     up2(S.T0, t0a, t0b);
     up2(S.U0, u0a, u0b);
@@ -1258,7 +1375,7 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
     }
     ch[0] += __shfl_xor_sync(0xffffffffu, ch[0], 2);
     ch[0] += __shfl_xor_sync(0xffffffffu, ch[0], 1);
-    const int64_t slot = p.goff[F.g_base + cur] + (int64_t)(tr - b.x) * (b.w - b.z + 1) + (tc - b.z);
+    const int64_t slot = go + (tr - b.x) * (b.w - b.z + 1) + (tc - b.z);
     if (slot >= 0 && slot < p.part_cap) {
       if ((lane & 3) == 0) reinterpret_cast<float*>(p.partials)[8 * slot + my_ch] = ch[0];
     } else if (lane == 0) {
@@ -1517,6 +1634,9 @@ void fill_params(Params<NF>& P, const gf_config* cfg, const gf_batch* batch, con
     d.vec_ok = ((reinterpret_cast<uintptr_t>(s.delta) & 15u) == 0) &&
                ((reinterpret_cast<uintptr_t>(s.base_weight) & 15u) == 0) && (s.in_features % (int64_t)vec == 0) &&
                (cfg->tile_in % (int64_t)vec == 0);
+    const int64_t gvec = cfg->grad_dtype == GF_BF16 ? 8 : 4;
+    d.gvec_ok = ((reinterpret_cast<uintptr_t>(s.grad_delta) & 15u) == 0) && (s.in_features % gvec == 0) &&
+                (cfg->tile_in % gvec == 0);
   }
 }
 
@@ -1582,7 +1702,7 @@ gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout&
 #define GF_FWD(N, C, O)                                                                         \
   do {                                                                                          \
     if (fast32 && O == GF_BF16 && (p.cfg.flags & GF_CFG_FWD_EXP2))                               \
-      render_fwd32_kernel<NF, N, C, O, (O == GF_BF16)><<<grid, 32 * kFwd32Warps, 0, st>>>(p);   \
+      render_fwd32_kernel<NF, N, C, O, (O == GF_BF16)><<<grid, 32 * fwd32_warps<(O == GF_BF16)>(), 0, st>>>(p); \
     else if (fast32) render_fwd32_kernel<NF, N, C, O, false><<<grid, 32 * kFwd32Warps, 0, st>>>(p); \
     else render_fwd_kernel<NF, N, C, O><<<grid, kRenderThreads, 0, st>>>(p);                    \
   } while (0)
@@ -1883,7 +2003,7 @@ gf_status noalloc_launch(Params<NF>& p, const gf_config* cfg, const gf_batch* ba
 #define GF_FWD(N, C, O)                                                                         \
   do {                                                                                          \
     if (fast32 && O == GF_BF16 && (p.cfg.flags & GF_CFG_FWD_EXP2))                               \
-      render_fwd32_kernel<NF, N, C, O, (O == GF_BF16)><<<grid, 32 * kFwd32Warps, 0, st>>>(p);   \
+      render_fwd32_kernel<NF, N, C, O, (O == GF_BF16)><<<grid, 32 * fwd32_warps<(O == GF_BF16)>(), 0, st>>>(p); \
     else if (fast32) render_fwd32_kernel<NF, N, C, O, false><<<grid, 32 * kFwd32Warps, 0, st>>>(p); \
     else render_fwd_kernel<NF, N, C, O><<<grid, kRenderThreads, 0, st>>>(p);                    \
   } while (0)

@@ -53,49 +53,113 @@ def lpt_partition(costs, world: int) -> list[list[int]]:
     return [sorted(p) for p in parts]
 
 
+def split_groups(costs, ng: int) -> list[int]:
+    """Bounds of ``ng`` contiguous runs of ``costs`` with balanced sums
+    (fewer when there are fewer items): [0, b1, ..., len(costs)]."""
+    n = len(costs)
+    ng = max(1, min(ng, n))
+    total, bounds, acc, g = sum(costs), [0], 0, 1
+    for j, c in enumerate(costs):
+        acc += c
+        if g < ng and acc >= total * g / ng and j + 1 < n:
+            bounds.append(j + 1)
+            g += 1
+    bounds.append(n)
+    return bounds
+
+
 @dataclass
 class GatherLayout:
-    """Where each field's delta lives in the [world, slot] gather buffer."""
+    """Where each field's delta lives in the flat gather buffer.
+
+    Each rank's fields (``parts[r]``, ascending) are split into ``groups``
+    contiguous runs balanced by render cost (``costs``; by size when absent).
+    The buffer is group-major: group g occupies ``[base[g], base[g] + world *
+    slot[g])``, rank r's share of it the chunk ``base[g] + r * slot[g]`` with
+    ``slot[g]`` = the largest rank's share, padded to 64 elements (128 B).  So
+    every group is one contiguous all-gather (in place: each rank's chunk is
+    its input), which can run as soon as that group is rendered, and the
+    fields of a chunk are packed in the rank's field order.  Every rank
+    computes the same layout from the same lists."""
 
     parts: list[list[int]]
     numels: list[int]
+    groups: int = 1
+    costs: list[int] | None = None
 
     def __post_init__(self):
-        self.owner = {}
-        self.offset = {}
-        self.rank_numel = []
+        world = len(self.parts)
+        G = max(1, int(self.groups))
+        self.owner, self.group_of, self.offset = {}, {}, {}
+        self.rank_groups: list[list[list[int]]] = []   # [rank][group] -> fields
+        chunk = [[0] * G for _ in range(world)]
+        within = {}
         for r, fs in enumerate(self.parts):
-            off = 0
-            for f in fs:
-                self.owner[f] = r
-                self.offset[f] = off
-                off += self.numels[f]
-            self.rank_numel.append(off)
-        # pad the slot to a multiple of 64 elements (128 B) for aligned rows
-        self.slot = max(1, max(self.rank_numel))
-        self.slot = (self.slot + 63) // 64 * 64
+            fs = list(fs)
+            w = [max(1, (self.costs[f] if self.costs is not None else self.numels[f])) for f in fs]
+            b = split_groups(w, G) if fs else [0, 0]
+            runs = [fs[b[k]:b[k + 1]] for k in range(len(b) - 1)]
+            runs += [[] for _ in range(G - len(runs))]
+            self.rank_groups.append(runs)
+            for g, run in enumerate(runs):
+                off = 0
+                for f in run:
+                    self.owner[f], self.group_of[f] = r, g
+                    within[f] = off
+                    off += self.numels[f]
+                chunk[r][g] = off
+        self.chunk_numel = chunk
+        self.slot = [(max(chunk[r][g] for r in range(world)) + 63) // 64 * 64 for g in range(G)]
+        self.base = [0]
+        for g in range(G):
+            self.base.append(self.base[-1] + world * self.slot[g])
+        self.total = self.base[-1]
+        for f in self.owner:
+            g, r = self.group_of[f], self.owner[f]
+            self.offset[f] = self.base[g] + r * self.slot[g] + within[f]
+        self.rank_numel = [sum(chunk[r]) for r in range(world)]
 
     @property
     def world(self) -> int:
         return len(self.parts)
 
+    @property
+    def num_groups(self) -> int:
+        return len(self.slot)
+
     def field_view(self, gathered: torch.Tensor, f: int) -> torch.Tensor:
-        r, off = self.owner[f], self.offset[f]
-        return gathered[r, off:off + self.numels[f]]
+        off = self.offset[f]
+        return gathered.view(-1)[off:off + self.numels[f]]
+
+    def chunk(self, gathered: torch.Tensor, g: int, r: int) -> torch.Tensor:
+        """Rank r's share of group g (slot[g] elements, its fields first)."""
+        b = self.base[g] + r * self.slot[g]
+        return gathered.view(-1)[b:b + self.slot[g]]
+
+    def group_span(self, gathered: torch.Tensor, g: int) -> torch.Tensor:
+        return gathered.view(-1)[self.base[g]:self.base[g + 1]]
 
 
-def all_gather_slots(gathered: torch.Tensor, rank: int, group=None) -> None:
-    """In-place all-gather of slot ``rank`` of ``gathered`` [world, slot].
+def all_gather_group(gathered: torch.Tensor, layout: GatherLayout, g: int, rank: int, group=None) -> None:
+    """In-place all-gather of group g: every rank contributes its chunk.
 
-    NCCL takes the rank's slot as input directly (in-place form); other
+    NCCL takes the rank's chunk as input directly (in-place form); other
     backends (gloo, used by the CPU tests) gather into the row views."""
-    backend = dist.get_backend(group)
-    if backend == "nccl":
-        dist.all_gather_into_tensor(gathered.view(-1), gathered[rank], group=group)
+    if layout.slot[g] == 0:
+        return
+    span = layout.group_span(gathered, g)
+    mine = layout.chunk(gathered, g, rank)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(span, mine, group=group)
     else:
-        rows = list(gathered.unbind(0))
-        send = gathered[rank].clone()
-        dist.all_gather(rows, send, group=group)
+        rows = list(span.view(layout.world, layout.slot[g]).unbind(0))
+        dist.all_gather(rows, mine.clone(), group=group)
+
+
+def all_gather_slots(gathered: torch.Tensor, layout: GatherLayout, rank: int, group=None) -> None:
+    """All-gather of every group, in group order."""
+    for g in range(layout.num_groups):
+        all_gather_group(gathered, layout, g, rank, group)
 
 
 class PartitionedRenderer:
@@ -103,28 +167,27 @@ class PartitionedRenderer:
 
     ``shapes`` are (out, in, K) of every field of the model; ``costs`` their
     render costs (:func:`field_costs`); all ranks pass the same lists.  This
-    rank renders its fields (``own``) into its slot of ``gathered``
-    ``[world, slot]`` (bf16), and every rank ends the step with the whole
-    model's delta.
+    rank renders its fields (``own``) into its chunks of the flat bf16 gather
+    buffer ``gathered`` (:class:`GatherLayout`), and every rank ends the step
+    with the whole model's delta.
 
-    Exchange.  Where the GPUs share an NVLink multicast (NVLS) domain, the
-    gather buffer is allocated in symmetric memory and each rank *publishes*
-    its slot: the forward runs in ``groups`` launches over disjoint field
-    groups, and after each one a small side-stream kernel
-    (``gf_multicast_store``, 64 CTAs) writes that group's delta to the
-    multicast address, so the switch delivers it to every GPU once while the
-    next group renders and while the backward (which does not read the
-    gathered delta) runs.  A symmetric-memory barrier ends the exchange.
-    Elsewhere it falls back to one in-place NCCL all-gather on the side
-    stream, overlapped with the backward.
+    The forward runs in ``groups`` launches over disjoint field groups
+    (contiguous runs of ``own``, balanced by cost).  As soon as a group is
+    rendered its exchange starts on a side stream, so it overlaps the next
+    groups' render and the backward (which does not read the gathered delta):
 
-    ``fused=True`` (multicast only) removes the separate publish: the render
-    kernel itself stores every output row through the multicast address
-    (``gf_field.delta_multicast``), so the transfer leaves tile by tile while
-    the render computes.  The step then bins, starts the backward on the side
-    stream as soon as the binning is done (it overlaps the render, which waits
-    on NVLink ingress more than on arithmetic), renders with multicast stores,
-    and ends with the symmetric-memory barrier.
+    * NCCL (default): one in-place ``all_gather_into_tensor`` per group, issued
+      in group order on every rank;
+    * NVLink multicast (``use_multicast=True``, where the GPUs share an NVLS
+      domain): the buffer is symmetric memory and a small side-stream kernel
+      (``gf_multicast_store``, ``publish_blocks`` CTAs) writes the group's
+      chunk to the multicast address, so the switch delivers it to every GPU
+      once; a symmetric-memory barrier ends the exchange;
+    * ``fused=True`` (multicast only, one group): the render kernel itself
+      stores every output row through the multicast address
+      (``gf_field.delta_multicast``); the step bins, starts the backward on the
+      side stream as soon as the binning is done, renders with multicast
+      stores, and ends with the barrier.
     """
 
     def __init__(self, shapes, costs, rank: int, world: int, group=None, device=None, groups: int = 4,
@@ -137,7 +200,8 @@ class PartitionedRenderer:
         self.parts = lpt_partition(costs, world)
         self.own = self.parts[rank]
         numels = [int(o) * int(i) for o, i, _ in shapes]
-        self.layout = GatherLayout(self.parts, numels)
+        ng = 1 if (world == 1 or fused) else max(1, int(groups))
+        self.layout = GatherLayout(self.parts, numels, groups=ng, costs=list(costs))
         dev = device or torch.device("cuda", torch.cuda.current_device())
         self.device = dev
         out_dtype = batch_kw.pop("out_dtype", torch.bfloat16)
@@ -145,48 +209,43 @@ class PartitionedRenderer:
         self.publish_blocks = publish_blocks
         self.symm = None
         self.mc_ptr = 0
-        if world > 1 and use_multicast is not False:
+        n_buf = max(1, self.layout.total)
+        if world > 1 and (use_multicast or fused):
             try:
                 import torch.distributed._symmetric_memory as symm_mem
 
-                buf = symm_mem.empty(world * self.layout.slot, dtype=out_dtype, device=dev)
+                buf = symm_mem.empty(n_buf, dtype=out_dtype, device=dev)
                 hdl = symm_mem.rendezvous(buf, self.group.group_name)
                 if hdl.multicast_ptr:
                     buf.zero_()
                     self.symm, self.mc_ptr = hdl, int(hdl.multicast_ptr)
-                    self.gathered = buf.view(world, self.layout.slot)
+                    self.gathered = buf
             except (RuntimeError, AttributeError, ImportError):
                 self.symm = None
-            if (use_multicast or fused) and self.symm is None:
-                raise RuntimeError("NVLink multicast is not available for this group")
+        if (use_multicast or fused) and world > 1 and self.symm is None:
+            raise RuntimeError("NVLink multicast is not available for this group")
         if self.symm is None:
-            self.gathered = torch.zeros(world, self.layout.slot, dtype=out_dtype, device=dev)
+            self.gathered = torch.zeros(n_buf, dtype=out_dtype, device=dev)
         self.fused = bool(fused) and self.symm is not None
         self.exchange = ("nvls-multicast-fused-render" if self.fused else "nvls-multicast") if self.symm is not None \
             else ("nccl-all-gather" if world > 1 else "none")
-        # field groups: contiguous runs of this rank's fields (slot order), balanced by cost
-        own_costs = [max(1, costs[i]) for i in self.own]
-        ng = max(1, min(groups if self.symm is not None and not self.fused else 1, len(self.own)))
-        total, bounds, acc, g = sum(own_costs), [0], 0, 1
-        for j, c in enumerate(own_costs):
-            acc += c
-            if g < ng and acc >= total * g / ng and j + 1 < len(self.own):
-                bounds.append(j + 1)
-                g += 1
-        bounds.append(len(self.own))
-        self.group_bounds = bounds
-        self.batches, self.k_off, self.n_off = [], [0], [0]
-        for g0, g1 in zip(bounds[:-1], bounds[1:]):
-            fs = self.own[g0:g1]
-            n0 = self.n_off[-1]
-            n1 = n0 + sum(numels[i] for i in fs)
+        # one FieldBatch per non-empty group of this rank; parameters and
+        # gradients stay packed in ``own`` order (groups are runs of it)
+        self.batches, self.batch_group, self.k_off, self.n_off = [], [], [0], [0]
+        by_field = {f: (int(shapes[f][0]), int(shapes[f][1]), int(shapes[f][2])) for f in self.own}
+        for g, run in enumerate(self.layout.rank_groups[rank]):
+            if not run:
+                continue
+            n0, n1 = self.n_off[-1], self.n_off[-1] + sum(numels[f] for f in run)
+            dst = self.layout.chunk(self.gathered, g, rank)[:n1 - n0]
             mc = None
             if self.fused:
-                mc = self.mc_ptr + (rank * self.layout.slot + n0) * self.gathered.element_size()
-            self.batches.append(FieldBatch([shapes[i] for i in fs], out_dtype=out_dtype, device=dev,
-                                           delta_out=self.gathered[rank, n0:n1], delta_multicast=mc, **batch_kw))
+                mc = self.mc_ptr + (self.layout.base[g] + rank * self.layout.slot[g]) * self.gathered.element_size()
+            self.batches.append(FieldBatch([by_field[f] for f in run], out_dtype=out_dtype, device=dev,
+                                           delta_out=dst, delta_multicast=mc, **batch_kw))
+            self.batch_group.append(g)
             self.n_off.append(n1)
-            self.k_off.append(self.k_off[-1] + sum(int(shapes[i][2]) for i in fs))
+            self.k_off.append(self.k_off[-1] + sum(by_field[f][2] for f in run))
         self.side = torch.cuda.Stream(device=dev) if world > 1 else None
         self.gather_events = None  # optional list of (start, end) event pairs to record into
         self.graph = None
@@ -195,10 +254,20 @@ class PartitionedRenderer:
         """Flat delta of any field of the model (valid after :meth:`step`)."""
         return self.layout.field_view(self.gathered, f)
 
+    def field_grads(self, f: int, outs):
+        """(d_mu, d_chol_raw, d_amp) of own field ``f`` from :meth:`step`'s result."""
+        g = self.layout.group_of[f]
+        i = self.batch_group.index(g)
+        run = self.layout.rank_groups[self.rank][g]
+        k_field = self.batches[i].shapes
+        k0 = sum(k_field[j].num_gaussians for j in range(run.index(f)))
+        k = k_field[run.index(f)].num_gaussians
+        return tuple(t[k0:k0 + k] for t in outs[i])
+
     def ensure_capacity(self, mu, chol_raw, amp):
         grew = False
-        for g, b in enumerate(self.batches):
-            k0, k1 = self.k_off[g], self.k_off[g + 1]
+        for i, b in enumerate(self.batches):
+            k0, k1 = self.k_off[i], self.k_off[i + 1]
             while b.ensure_capacity(mu[k0:k1], chol_raw[k0:k1], amp[k0:k1]):
                 grew = True
         return grew
@@ -211,12 +280,19 @@ class PartitionedRenderer:
 
     def _publish(self, g: int):
         elt = self.gathered.element_size()
-        n0, n1 = self.n_off[g], self.n_off[g + 1]
-        nbytes = ((n1 - n0) * elt + 15) // 16 * 16
-        base = self.rank * self.layout.slot + n0
-        src = self.gathered.data_ptr() + base * elt
-        self._lib.check(self._lib.lib().gf_multicast_store(src, self.mc_ptr + base * elt, nbytes,
+        nbytes = (self.layout.chunk_numel[self.rank][g] * elt + 15) // 16 * 16
+        if nbytes == 0:
+            return
+        off = (self.layout.base[g] + self.rank * self.layout.slot[g]) * elt
+        self._lib.check(self._lib.lib().gf_multicast_store(self.gathered.data_ptr() + off, self.mc_ptr + off, nbytes,
                                                            self.publish_blocks, self.side.cuda_stream))
+
+    def _exchange_group(self, g: int):
+        """Issue group g's exchange on the side stream (after this rank's render of it)."""
+        if self.symm is not None:
+            self._publish(g)
+        else:
+            all_gather_group(self.gathered, self.layout, g, self.rank, self.group)
 
     def _step_fused(self, mu, chol_raw, amp, grad):
         from guass_b200 import _lib
@@ -248,31 +324,35 @@ class PartitionedRenderer:
         ev = None
         if self.world > 1 and self.gather_events is not None:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-        for g, b in enumerate(self.batches):
-            k0, k1 = self.k_off[g], self.k_off[g + 1]
+        nxt = 0  # next group to exchange (every rank exchanges every group, in order)
+        for i, b in enumerate(self.batches):
+            k0, k1 = self.k_off[i], self.k_off[i + 1]
             b.forward(mu[k0:k1], chol_raw[k0:k1], amp[k0:k1])
-            if self.symm is not None:
+            if self.world > 1:
                 self.side.wait_stream(main)
                 with torch.cuda.stream(self.side):
-                    if g == 0 and ev is not None:
+                    if nxt == 0 and ev is not None:
                         ev[0].record()
-                    self._publish(g)
+                    while nxt <= self.batch_group[i]:
+                        self._exchange_group(nxt)
+                        nxt += 1
         if self.world > 1:
+            self.side.wait_stream(main)
             with torch.cuda.stream(self.side):
+                if nxt == 0 and ev is not None:
+                    ev[0].record()
+                while nxt < self.layout.num_groups:
+                    self._exchange_group(nxt)
+                    nxt += 1
                 if self.symm is not None:
                     self.symm.barrier()
-                else:
-                    self.side.wait_stream(main)
-                    if ev is not None:
-                        ev[0].record()
-                    all_gather_slots(self.gathered, self.rank, self.group)
                 if ev is not None:
                     ev[1].record()
                     self.gather_events.append(ev)
         outs = []
-        for g, b in enumerate(self.batches):
-            k0, k1 = self.k_off[g], self.k_off[g + 1]
-            n0, n1 = self.n_off[g], self.n_off[g + 1]
+        for i, b in enumerate(self.batches):
+            k0, k1 = self.k_off[i], self.k_off[i + 1]
+            n0, n1 = self.n_off[i], self.n_off[i + 1]
             outs.append(b.backward(grad[n0:n1], mu[k0:k1], chol_raw[k0:k1], amp[k0:k1]))
         if self.world > 1:
             main.wait_stream(self.side)

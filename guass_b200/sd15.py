@@ -347,6 +347,8 @@ class DataParallelTrainer:
         self.params = adapter_parameters(self.mods)
         self.opt = torch.optim.AdamW(self.params, lr=lr)
         self.alphas_cumprod = noise_schedule(self.params[0].device)
+        # optional list of (start, end) CUDA events around each step's all-reduce
+        self.allreduce_events = None
 
     def backward(self, inputs: StepInputs) -> torch.Tensor:
         """Render, forward, backward and gradient all-reduce (no optimizer step)."""
@@ -356,7 +358,14 @@ class DataParallelTrainer:
         loss = diffusion_loss(self.model, inputs, self.alphas_cumprod)
         loss.backward()
         if self.world > 1:
+            ev = None
+            if self.allreduce_events is not None:
+                ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                ev[0].record()
             allreduce_adapter_grads(self.mods, group=self.group)
+            if ev is not None:
+                ev[1].record()
+                self.allreduce_events.append(ev)
         return loss.detach()
 
     def step(self, inputs: StepInputs) -> torch.Tensor:

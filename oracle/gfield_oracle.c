@@ -284,8 +284,11 @@ static void pair_partials(int64_t t, int64_t g, int64_t out_features,
       if (q_active) {
         const float coeff = common * -0.5f;
         const float sym01 = i01 + i10;
-        const float dq0 = -(2.0f * i00 * dx + sym01 * dy);
-        const float dq1 = -(sym01 * dx + 2.0f * i11 * dy);
+        /* :338-339 as the reference's nvcc build contracts them (one fma,
+         * the dy product inside it); tests/test_gpu_reference_ext.py pins this
+         * rounding against the reference extension on single-element fields */
+        const float dq0 = -fmaf(sym01, dy, 2.0f * i00 * dx);
+        const float dq1 = -fmaf(2.0f * i11, dy, sym01 * dx);
         const float dxdy = dx * dy;
         term[1] = coeff * dq0;
         term[2] = coeff * dq1;

@@ -44,7 +44,7 @@ def _worker(rank, world, port, use_mc, q):
         costs = [f.numel for f in fields]
         fused = use_mc == "fused"
         try:
-            r = PartitionedRenderer(shapes, costs, rank, world, groups=3, use_multicast=None if fused else use_mc,
+            r = PartitionedRenderer(shapes, costs, rank, world, groups=3, use_multicast=(use_mc == "multicast"),
                                     fused=fused)
         except RuntimeError as exc:
             if "multicast is not available" not in str(exc):
@@ -65,19 +65,15 @@ def _worker(rank, world, port, use_mc, q):
                 ok, msg = False, f"delta of field {i} differs"
             if i in r.own:
                 dm, dc, da = fb.backward(g1, m1, c1, a1)
-                g = r.own.index(i)
-                gi = next(j for j in range(len(r.batches)) if r.group_bounds[j] <= g < r.group_bounds[j + 1])
-                k0 = sum(fields[r.own[j]].k for j in range(r.group_bounds[gi], g))
-                got = outs[gi]
-                if not (torch.equal(got[0][k0:k0 + f.k], dm) and torch.equal(got[1][k0:k0 + f.k], dc)
-                        and torch.equal(got[2][k0:k0 + f.k], da)):
+                got = r.field_grads(i, outs)
+                if not (torch.equal(got[0], dm) and torch.equal(got[1], dc) and torch.equal(got[2], da)):
                     ok, msg = False, f"gradients of field {i} differ"
         q.put((rank, ok, msg, r.exchange))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("use_mc", [None, False, "fused"])
+@pytest.mark.parametrize("use_mc", ["multicast", "nccl", "fused"])
 def test_partitioned_render_two_gpus(use_mc):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -90,7 +86,7 @@ def test_partitioned_render_two_gpus(use_mc):
     for p in procs:
         p.join(timeout=300)
     res = [q.get(timeout=30) for _ in procs]
-    if use_mc == "fused" and any("multicast is not available" in m for _, _, m, _ in res):
+    if use_mc != "nccl" and any("multicast is not available" in m for _, _, m, _ in res):
         pytest.skip("no NVLink multicast between these GPUs")
     assert all(p.exitcode == 0 for p in procs)
     for rank, ok, msg, exchange in res:

@@ -97,3 +97,48 @@ def test_binning_bit_exact_at_scale(ref_ext):
     assert torch.equal(mine[1], theirs[1])
     assert torch.equal(mine[2], theirs[2])
     assert torch.equal(mine[0].view(torch.int32), theirs[0].view(torch.int32))
+
+
+def test_reference_dq_rounding_is_the_contracted_form(ref_ext):
+    """The per-element mu factor dq/dmu = -(2*A00*dx + 2*A01*dy)
+    (backward.cu:338-339) as the reference's build rounds it: on single-element
+    fields its d_mu is one float term coeff*dq, so d_mu0/dq0 == d_mu1/dq1 must
+    hold for the form the oracle and these kernels use,
+    dq0 = -fma(2*A01, dy, 2*A00*dx), dq1 = -fma(2*A11, dy, 2*A01*dx)."""
+    import math
+
+    from gpu_helpers import device_geometry
+    from guass_b200.synthetic import FieldInputs
+
+    f32 = np.float32
+
+    def fma(a, b, c):
+        return f32(np.float64(a) * np.float64(b) + np.float64(c))
+
+    rng = np.random.default_rng(0)
+    checked = agree = 0
+    for _ in range(120):
+        mu = torch.tensor([[rng.uniform(-1.3, -0.7), rng.uniform(-1.3, -0.7)]], dtype=torch.float32)
+        chol = torch.tensor([[rng.normal(-2, 1), rng.normal(0, 0.3), rng.normal(-2, 1)]], dtype=torch.float32)
+        f = FieldInputs(1, 1, torch.tensor([-1.0]), torch.tensor([-1.0]), mu, chol,
+                        torch.ones(1, 1), torch.ones(1))
+        d = f.to("cuda")
+        _, tp, ids = ref_ext.gaussian_field_forward(d.row_coords, d.col_coords, d.mu, d.chol_raw, d.amp, 32, 32,
+                                                    3.0, False, None)
+        if int(tp[-1]) != 1:
+            continue
+        dm = ref_ext.gaussian_field_backward(d.grad, d.row_coords, d.col_coords, d.mu, d.chol_raw, d.amp, tp, ids,
+                                             32, 32, 3.0, False, None)[0].cpu().numpy()[0]
+        inv, _ = device_geometry(f)
+        i00, i01, i11 = f32(inv[0, 0, 0]), f32(inv[0, 0, 1]), f32(inv[0, 1, 1])
+        dx, dy = f32(f32(-1.0) - mu[0, 0].item()), f32(f32(-1.0) - mu[0, 1].item())
+        sym = f32(i01 + i01)
+        dq0 = -fma(sym, dy, f32(f32(f32(2.0) * i00) * dx))
+        dq1 = -fma(f32(f32(2.0) * i11), dy, f32(sym * dx))
+        if dq0 == 0 or dq1 == 0 or not math.isfinite(dm[0] / dq0):
+            continue
+        checked += 1
+        c0, c1 = dm[0] / dq0, dm[1] / dq1
+        agree += abs(c0 - c1) <= 3e-7 * abs(c0)
+    assert checked >= 50
+    assert agree == checked, f"{checked - agree} of {checked} single-element fields disagree"

@@ -31,8 +31,32 @@ def test_lpt_partition_balanced_and_deterministic():
 def test_gather_layout_offsets():
     lay = GatherLayout([[0, 2], [1]], [10, 20, 30])
     assert lay.owner == {0: 0, 2: 0, 1: 1}
-    assert lay.offset == {0: 0, 2: 10, 1: 0}
-    assert lay.rank_numel == [40, 20] and lay.slot == 64
+    # one group: rank r's chunk starts at r * slot
+    assert lay.slot == [64] and lay.total == 128
+    assert lay.offset == {0: 0, 2: 10, 1: 64}
+    assert lay.rank_numel == [40, 20]
+
+
+def test_gather_layout_groups_are_contiguous_spans():
+    numels = [100, 30, 50, 70, 20, 90]
+    parts = [[0, 2, 4], [1, 3, 5]]
+    lay = GatherLayout(parts, numels, groups=2, costs=[10, 3, 5, 7, 2, 9])
+    assert lay.num_groups == 2
+    for r, runs in enumerate(lay.rank_groups):
+        assert [f for run in runs for f in run] == parts[r]  # runs of the rank's own order
+    seen = set()
+    for f, n in enumerate(numels):
+        g, r = lay.group_of[f], lay.owner[f]
+        lo = lay.base[g] + r * lay.slot[g]
+        assert lo <= lay.offset[f] and lay.offset[f] + n <= lo + lay.slot[g]  # inside its chunk
+        span = set(range(lay.offset[f], lay.offset[f] + n))
+        assert not (span & seen)
+        seen |= span
+    assert all(s % 64 == 0 for s in lay.slot) and lay.total == lay.base[-1]
+    # more groups than a rank has fields: empty runs, still one span per group
+    lay3 = GatherLayout([[0], [1, 2, 3]], [5, 5, 5, 5], groups=3)
+    assert [len(r) for r in lay3.rank_groups[0]] == [1, 0, 0]
+    assert lay3.num_groups == 3
 
 
 def _free_port():
@@ -43,28 +67,32 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, numels, parts, q):
+def _worker(rank, world, port, numels, parts, q, groups=1):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        lay = GatherLayout(parts, numels)
-        gathered = torch.zeros(world, lay.slot)
+        lay = GatherLayout(parts, numels, groups=groups)
+        gathered = torch.zeros(lay.total)
         for f in parts[rank]:  # each rank "renders" its own fields
             lay.field_view(gathered, f).fill_(float(f + 1))
-        all_gather_slots(gathered, rank)
+        all_gather_slots(gathered, lay, rank)
         ok = all(bool((lay.field_view(gathered, f) == f + 1).all()) for f in range(len(numels)))
         q.put((rank, ok))
     finally:
         dist.destroy_process_group()
 
 
-def test_all_gather_slots_on_gloo_ranks():
-    numels = [5, 7, 3, 9, 4]
+import pytest  # noqa: E402
+
+
+@pytest.mark.parametrize("groups", [1, 3])
+def test_all_gather_slots_on_gloo_ranks(groups):
+    numels = [5, 7, 3, 9, 4, 6, 8]
     parts = lpt_partition(numels, 2)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, numels, parts, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, numels, parts, q, groups)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
@@ -80,12 +108,12 @@ def _dying_worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
     lay = GatherLayout([[0], [1]], [8, 8])
-    gathered = torch.zeros(world, lay.slot)
+    gathered = torch.zeros(lay.total)
     dist.barrier()
     if rank == 1:
         os._exit(0)  # the peer dies between steps, before the exchange
     try:
-        all_gather_slots(gathered, rank)
+        all_gather_slots(gathered, lay, rank)
         q.put((rank, "completed"))
     except Exception as exc:  # noqa: BLE001
         q.put((rank, type(exc).__name__))
