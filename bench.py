@@ -222,14 +222,13 @@ def run_device_timed(w: UNetWorkload, steps: int, warmup: int, world: int):
     for _ in range(warmup):
         w.step()
     torch.cuda.synchronize()
-    # per step: 3 trace events per forward call, then 4 per backward call (gfield.h, gf_trace_events)
-    G = len(w.renderer.batches)
-    per_step = 7 * G
+    # per step: the library's trace events in host call order (gfield.h, gf_trace_events)
+    per_step = w.renderer.trace_events_per_step()
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(per_step * steps)]
     for e in evs:
         e.record()
     torch.cuda.synchronize()
-    handles = (ctypes.c_void_p * len(evs))(*[e.cuda_event for e in evs])
+    handles = (ctypes.c_void_p * max(1, len(evs)))(*[e.cuda_event for e in evs])
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
@@ -246,27 +245,13 @@ def run_device_timed(w: UNetWorkload, steps: int, warmup: int, world: int):
     assert recorded == len(evs), (recorded, len(evs))
     ms = start.elapsed_time(end) / steps
     per = {n: [] for n in ("bin", "render_fwd", "bwd_prep", "render_bwd", "bwd_finalize")}
-    for s in range(steps):
-        e = evs[per_step * s: per_step * (s + 1)]
-        if w.renderer.fused:
-            # host call order: BIN stage (start, bin), backward on the side stream (start, prep,
-            # render, finalize), RENDER stage (render: from the end of binning, overlapping the backward)
-            per["bin"].append(e[0].elapsed_time(e[1]))
-            per["render_fwd"].append(e[1].elapsed_time(e[6]))
-            per["bwd_prep"].append(e[2].elapsed_time(e[3]))
-            per["render_bwd"].append(e[3].elapsed_time(e[4]))
-            per["bwd_finalize"].append(e[4].elapsed_time(e[5]))
-            continue
-        b = 3 * G
-        per["bin"].append(sum(e[3 * g].elapsed_time(e[3 * g + 1]) for g in range(G)))
-        per["render_fwd"].append(sum(e[3 * g + 1].elapsed_time(e[3 * g + 2]) for g in range(G)))
-        per["bwd_prep"].append(sum(e[b + 4 * g].elapsed_time(e[b + 4 * g + 1]) for g in range(G)))
-        per["render_bwd"].append(sum(e[b + 4 * g + 1].elapsed_time(e[b + 4 * g + 2]) for g in range(G)))
-        per["bwd_finalize"].append(sum(e[b + 4 * g + 2].elapsed_time(e[b + 4 * g + 3]) for g in range(G)))
+    for s_ in range(steps if per_step else 0):
+        for k, v in w.renderer.kernel_times(evs[per_step * s_: per_step * (s_ + 1)]).items():
+            per[k].append(v)
     if world > 1:
         per["exchange_side_stream"] = [a.elapsed_time(b) for a, b in w.renderer.gather_events]
         w.renderer.gather_events = None
-    kern = {k: sum(v) / len(v) for k, v in per.items()}
+    kern = {k: (sum(v) / len(v) if v else 0.0) for k, v in per.items()}  # same keys on every rank
     return ms, kern
 
 
@@ -971,11 +956,12 @@ def main():
         "e2e_dropin_per_layer": e2e_layer,
         "cpu_baseline": cpu,
         **extra,
-        # per field group: bin, render, prep, backward render, finalize (+ the publish kernel of the
-        # multicast exchange; the fused exchange stores from the render itself)
-        "gpu_launches": (5 * len(w.renderer.batches)
-                         + (len(w.renderer.batches) if w.renderer.symm is not None and not w.renderer.fused else 0))
-                        * a.steps * world,
+        # per step: bin (+ the id lists when the render runs in field groups), one render per group,
+        # prep, backward render, finalize, (+ one publish kernel per group of the multicast exchange)
+        "gpu_launches": a.steps * world * (
+            5 if world == 1 else (2 + (1 if w.renderer.fused else len(w.renderer.ranges)) + 3
+                                  + (w.layout.num_groups if w.renderer.symm is not None and not w.renderer.fused
+                                     else 0))),
     }
     print(json.dumps(line), flush=True)
     if world > 1:

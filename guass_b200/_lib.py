@@ -47,7 +47,7 @@ GF_FLAG_BOUNDS = 0x8
 EXPORTED = ("gf_abi_version", "gf_last_error", "gf_num_tiles", "gf_workspace_bytes", "gf_forward",
             "gf_backward", "gf_workspace_status", "gf_trace_events", "gf_trace_count",
             "gf_forward_noalloc", "gf_multicast_store", "gf_grad_stats_accumulate",
-            "gf_forward_stages")
+            "gf_forward_stages", "gf_forward_render_fields")
 
 
 class GfConfig(ctypes.Structure):
@@ -155,6 +155,9 @@ def lib() -> ctypes.CDLL:
     L.gf_forward_stages.argtypes = [ctypes.POINTER(GfConfig), ctypes.POINTER(GfBatch), ctypes.c_void_p,
                                     ctypes.c_size_t, ctypes.c_uint, ctypes.c_void_p]
     L.gf_forward_stages.restype = ctypes.c_int
+    L.gf_forward_render_fields.argtypes = [ctypes.POINTER(GfConfig), ctypes.POINTER(GfBatch), ctypes.c_void_p,
+                                           ctypes.c_size_t, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]
+    L.gf_forward_render_fields.restype = ctypes.c_int
     if L.gf_abi_version() != GF_ABI_VERSION:
         raise ImportError(f"libgfield ABI {L.gf_abi_version()} != expected {GF_ABI_VERSION}")
     _lib = L

@@ -29,12 +29,13 @@ import torch.nn.functional as F
 from torch import nn
 
 
-# Pair capacity: the exact upper bound (every Gaussian in every tile of its
-# field) costs 8 bytes of ids plus 32 bytes of backward partials per pair; up
-# to this many pairs (1.6 GB) it is reserved outright and no pair count can
-# overflow; an SD1.5 UNet with K=256 needs 23.4 M.  Larger batches measure
-# their pair count on the first render (and on ensure_capacity()).
-MAX_BOUND_PAIRS = 40_000_000
+# Pair capacity: the id buffer is reserved at the exact upper bound (every
+# Gaussian in every tile of its field, 8 bytes per possible pair) up to this
+# many pairs (128 MB), so no pair count can overflow it; an SD1.5 UNet with
+# K=256 needs 23.4 M and measures instead.  Batches above it measure their
+# pair count on the first render (and on ensure_capacity()).  The backward's
+# pair partials (32 bytes per pair) follow the actual pair count, not the bound.
+MAX_BOUND_PAIRS = 16_000_000
 
 
 def pair_bound(shapes, tile_out: int, tile_in: int) -> int:

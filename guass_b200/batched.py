@@ -44,7 +44,7 @@ class FieldBatch:
                  grad_dtype=torch.float32, out_scale: float = 1.0, device="cuda", ids_capacity: int | None = None,
                  row_coords=None, col_coords=None, delta_out: torch.Tensor | None = None,
                  base_weight: torch.Tensor | None = None, delta_multicast: int | None = None,
-                 bwd_exp2: bool = False, fwd_exp2: bool = False):
+                 bwd_exp2: bool = False, fwd_exp2: bool = False, field_outputs=None):
         self.shapes = [s if isinstance(s, FieldShape) else FieldShape(*s) for s in shapes]
         n = len(self.shapes)
         if not 1 <= n <= _lib.GF_MAX_FIELDS:
@@ -80,7 +80,24 @@ class FieldBatch:
             col_coords = [torch.linspace(-1.0, 1.0, s.in_features, dtype=torch.float32) for s in self.shapes]
         self.row = torch.cat([r.reshape(-1).float().cpu() for r in row_coords]).to(dev)
         self.col = torch.cat([c.reshape(-1).float().cpu() for c in col_coords]).to(dev)
-        if delta_out is not None:
+        # field_outputs: one contiguous out_dtype tensor per field (out*in elements each, anywhere in
+        # memory) that the forward writes instead of a packed delta; ``self.delta`` is then None
+        self._field_out = None
+        self._esz_out = torch.empty(0, dtype=out_dtype).element_size()
+        if field_outputs is not None:
+            if delta_out is not None or delta_multicast:
+                raise ValueError("field_outputs excludes delta_out and delta_multicast")
+            outs = list(field_outputs)
+            if len(outs) != n:
+                raise ValueError(f"field_outputs needs {n} tensors, got {len(outs)}")
+            for t, sh in zip(outs, self.shapes):
+                if t.dtype != out_dtype or not t.is_contiguous() or t.device != dev or \
+                        t.numel() != sh.out_features * sh.in_features:
+                    raise ValueError(f"each field output must be a contiguous {out_dtype} tensor of out*in "
+                                     f"elements on {dev}")
+            self._field_out = outs
+            self.delta = None
+        elif delta_out is not None:
             if delta_out.dtype != out_dtype or delta_out.numel() < self.n_off[-1] or not delta_out.is_contiguous():
                 raise ValueError(f"delta_out must be a contiguous {out_dtype} tensor of >= {self.n_off[-1]} elements")
             self.delta = delta_out.view(-1)[:self.n_off[-1]]
@@ -96,6 +113,10 @@ class FieldBatch:
         self.d_amp = torch.empty(total_g, 1, dtype=torch.float32, device=dev)
         self._ws = None      # forward workspace
         self._ws_bwd = None  # backward workspace (separate, so a backward may overlap a render)
+        # the last binning's pair count on its way to the host (pinned copy + event): an eager
+        # backward sizes its pair partials (32 bytes per pair) by it instead of the id capacity
+        self._count_host = torch.empty(1, dtype=torch.int64, pin_memory=dev.type == "cuda")
+        self._count_done = None
         self._bound = None
         self._grad_bound = None
         self._out_bound = None
@@ -115,7 +136,7 @@ class FieldBatch:
         the all-gather in one kernel).  The caller runs a group barrier before
         any GPU reads the result.  ``None`` restores local stores."""
         self.delta_multicast = int(address) if address else None
-        esz = self.delta.element_size()
+        esz = self._esz_out
         for f in range(len(self.shapes)):
             self._fields[f].delta_multicast = None if not address else int(address) + esz * self.n_off[f]
 
@@ -139,7 +160,7 @@ class FieldBatch:
                 raise ValueError(f"base_weight must be a contiguous {self.out_dtype} tensor of {self.numel()} "
                                  f"elements on {self.device}")
         self.base_weight = base_weight
-        esz = self.delta.element_size()
+        esz = self._esz_out
         for f in range(len(self.shapes)):
             self._fields[f].base_weight = None if base_weight is None else base_weight.data_ptr() + esz * self.n_off[f]
 
@@ -155,6 +176,8 @@ class FieldBatch:
 
     def delta_view(self, f: int) -> torch.Tensor:
         s = self.shapes[f]
+        if self._field_out is not None:
+            return self._field_out[f].view(s.out_features, s.in_features)
         return self.delta[self.n_off[f]:self.n_off[f + 1]].view(s.out_features, s.in_features)
 
     def tile_ptr_view(self, f: int) -> torch.Tensor:
@@ -183,7 +206,7 @@ class FieldBatch:
                 raise RuntimeError(f"{name} must be a contiguous float32 tensor on {self.device}")
             if t.numel() != total_g * cols:
                 raise RuntimeError(f"{name} must have shape [{total_g}, {cols}]")
-        esz_out = self.delta.element_size()
+        esz_out = self._esz_out
         for f, s in enumerate(self.shapes):
             g0, n0 = self.g_off[f], self.n_off[f]
             fd = self._fields[f]
@@ -193,7 +216,8 @@ class FieldBatch:
             fd.mu = mu.data_ptr() + 8 * g0
             fd.chol_raw = chol_raw.data_ptr() + 12 * g0
             fd.amp = amp.data_ptr() + 4 * g0
-            fd.delta = self.delta.data_ptr() + esz_out * n0  # rebound per call by _bind_out
+            fd.delta = (self._field_out[f].data_ptr() if self._field_out is not None
+                        else self.delta.data_ptr() + esz_out * n0)  # rebound per call by _bind_out
             fd.tile_ptr = self.tile_ptr.data_ptr() + 8 * self.t_off[f]
             fd.gaussian_ids = None
             fd.ids_capacity = 0
@@ -203,16 +227,15 @@ class FieldBatch:
         self._batch.ids = self.ids.data_ptr()
         self._batch.ids_capacity = self.ids.numel()
         self._batch.pair_base = self.pair_base.data_ptr()
-        need_f, need_b = (self._lib.gf_workspace_bytes(ctypes.byref(self.cfg), ctypes.byref(self._batch), p)
-                          for p in (_lib.GF_PASS_FORWARD, _lib.GF_PASS_BACKWARD))
-        if need_f == 0 or need_b == 0:
+        need_f = self._lib.gf_workspace_bytes(ctypes.byref(self.cfg), ctypes.byref(self._batch),
+                                              _lib.GF_PASS_FORWARD)
+        if need_f == 0:
             raise RuntimeError("invalid batch: " + _lib.last_error())
         if self._ws is None or self._ws.numel() < need_f:
             self._ws = torch.zeros(need_f, dtype=torch.uint8, device=self.device)
-        if self._ws_bwd is None or self._ws_bwd.numel() < need_b:
-            self._ws_bwd = torch.zeros(need_b, dtype=torch.uint8, device=self.device)
         self._bound = key
-        self._out_bound = self.delta.data_ptr()  # the loop above pointed every field at self.delta
+        # the loop above pointed every field at self.delta (or at its own output)
+        self._out_bound = self.delta.data_ptr() if self.delta is not None else -1
 
     # -- passes --------------------------------------------------------------
     def forward(self, mu, chol_raw, amp, stream=None, out: torch.Tensor | None = None) -> torch.Tensor:
@@ -221,6 +244,17 @@ class FieldBatch:
         intact); no host synchronisation."""
         return self.forward_stages(mu, chol_raw, amp, _lib.GF_STAGE_BIN | _lib.GF_STAGE_RENDER, stream, out)
 
+    def forward_render_fields(self, mu, chol_raw, amp, first: int, count: int, stream=None) -> None:
+        """The RENDER stage for fields [first, first + count) only (after a BIN
+        stage of this batch): disjoint ranges may render in separate calls, so
+        that an exchange of one range's delta overlaps the next range."""
+        self._bind(mu, chol_raw, amp)
+        self._bind_out(None)
+        st = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        _lib.check(self._lib.gf_forward_render_fields(ctypes.byref(self.cfg), ctypes.byref(self._batch),
+                                                      self._ws.data_ptr(), self._ws.numel(), int(first), int(count),
+                                                      st))
+
     def forward_stages(self, mu, chol_raw, amp, stages: int, stream=None,
                        out: torch.Tensor | None = None) -> torch.Tensor:
         """``forward`` in stages (GF_STAGE_BIN, GF_STAGE_RENDER): a backward
@@ -228,12 +262,55 @@ class FieldBatch:
         the BIN stage is done and overlap the RENDER stage."""
         self._bind(mu, chol_raw, amp)
         dst = self._bind_out(out)
-        st = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        strm = stream or torch.cuda.current_stream(self.device)
         _lib.check(self._lib.gf_forward_stages(ctypes.byref(self.cfg), ctypes.byref(self._batch), self._ws.data_ptr(),
-                                               self._ws.numel(), int(stages), st))
+                                               self._ws.numel(), int(stages), strm.cuda_stream))
+        if stages & _lib.GF_STAGE_BIN:
+            self._probe_pairs(strm)
         return dst
 
+    def _probe_pairs(self, stream):
+        """Start the copy of this binning's pair count to the host (not
+        inside a CUDA-graph capture, whose replays could not adapt to it)."""
+        if torch.cuda.is_current_stream_capturing():
+            self._count_done = None
+            return
+        with torch.cuda.stream(stream):
+            self._count_host.copy_(self.pair_base[-1:], non_blocking=True)
+            self._count_done = torch.cuda.Event()
+            self._count_done.record(stream)
+
+    def reserve_backward_workspace(self) -> None:
+        """Size the backward workspace for the full id capacity now (call it
+        before capturing a backward into a CUDA graph, so that the capture
+        allocates and clears nothing)."""
+        done, self._count_done = self._count_done, None
+        self._backward_workspace()
+        self._count_done = done
+
+    def _backward_workspace(self) -> int:
+        """Size the backward workspace; returns the pair capacity to pass.
+        Eager: the last binning's pair count (read when the copy is long
+        done); under capture: the id capacity (a replay may see any count)."""
+        cap = self.ids.numel()
+        if self._count_done is not None and not torch.cuda.is_current_stream_capturing():
+            self._count_done.synchronize()
+            cap = max(1, min(cap, int(self._count_host[0])))
+        self._batch.ids_capacity = cap
+        need_b = self._lib.gf_workspace_bytes(ctypes.byref(self.cfg), ctypes.byref(self._batch),
+                                              _lib.GF_PASS_BACKWARD)
+        self._batch.ids_capacity = self.ids.numel()
+        if need_b == 0:
+            raise RuntimeError("invalid batch: " + _lib.last_error())
+        if self._ws_bwd is None or self._ws_bwd.numel() < need_b:
+            self._ws_bwd = torch.zeros(need_b, dtype=torch.uint8, device=self.device)
+        return cap
+
     def _bind_out(self, out):
+        if self._field_out is not None:
+            if out is not None:
+                raise RuntimeError("out= cannot be combined with field_outputs")
+            return None
         dst = self.delta if out is None else out
         if out is not None and (out.dtype != self.out_dtype or not out.is_contiguous() or out.numel() != self.numel()
                                 or out.device != self.device):
@@ -253,8 +330,13 @@ class FieldBatch:
         self._bind(mu, chol_raw, amp)
         self._bind_grad(grad)
         st = (stream or torch.cuda.current_stream(self.device)).cuda_stream
-        _lib.check(self._lib.gf_backward(ctypes.byref(self.cfg), ctypes.byref(self._batch),
-                                         self._ws_bwd.data_ptr(), self._ws_bwd.numel(), st))
+        cap = self._backward_workspace()
+        self._batch.ids_capacity = cap  # the backward reads ids[0, pairs) only
+        try:
+            _lib.check(self._lib.gf_backward(ctypes.byref(self.cfg), ctypes.byref(self._batch),
+                                             self._ws_bwd.data_ptr(), self._ws_bwd.numel(), st))
+        finally:
+            self._batch.ids_capacity = self.ids.numel()
         return self.d_mu, self.d_chol_raw, self.d_amp
 
     def device_flags(self, reset: bool = True) -> int:

@@ -85,7 +85,7 @@ struct Params {
   int32_t n;
   int32_t total_tiles;
   int32_t total_g;
-  int32_t pad_;
+  int32_t tile_offset;   // render kernels: first global tile of the launch (field-range renders)
   uint32_t* status;
   uint32_t* done;
   float4* records;       // [total_g][2]
@@ -433,7 +433,7 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
   __shared__ int s_list[kChunk];
   __shared__ int s_wcnt[8];
   __shared__ float s_out[32][33];
-  const int tg = blockIdx.x;
+  const int tg = blockIdx.x + p.tile_offset;
   const int fi = field_of_tile(p, tg);
   const DevField& F = p.f[fi];
   const int t = tg - F.tile_base;
@@ -673,7 +673,7 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
   constexpr int NW = fwd32_warps<EX2>();
   constexpr int R = 32 / NW;  // rows per warp
   __shared__ __align__(16) float s_out[NW][R][36];
-  const int tg = blockIdx.x;
+  const int tg = blockIdx.x + p.tile_offset;
   const int fi = field_of_tile(p, tg);
   const DevField& F = p.f[fi];
   const int t = tg - F.tile_base;
@@ -1108,11 +1108,11 @@ render_bwd_kernel(const __grid_constant__ Params<NF> p) {
 // ---------------------------------------------------------------------------
 // Backward kernel 2, 32x32-tile fast path: one CTA of kBwd32Warps warps per
 // tile; warp w handles the tile's pairs w, w+W, ...  The tile's dL/d(delta)
-// is staged once in shared memory, transposed (s_gt[col][row], row stride 34
-// floats so each lane's 64-bit read of two consecutive rows is conflict
-// free), next to the 32 row coordinates.  Lane = column; rows go in pairs
-// through packed fp32x2 arithmetic; the basis is evaluated exactly as in the
-// forward.  The six per-pair channels are reduced across the warp with a
+// is staged once in shared memory, transposed (s_gt[col][row], row stride 36
+// floats so each lane's 128-bit read of four consecutive rows is aligned and
+// conflict free), next to the 32 row coordinates.  Lane = column; rows go in
+// pairs through packed fp32x2 arithmetic; the quadratic form is evaluated
+// exactly as in the forward.  The six per-pair channels are reduced across the warp with a
 // reduce-scatter (9 shuffles instead of 30); lanes 0, 4, ..., 28 then hold
 // channels 0..7 and write the pair's slot with one 32-byte store.
 //
@@ -1129,13 +1129,15 @@ render_bwd_kernel(const __grid_constant__ Params<NF> p) {
 #ifndef GF_BWD32_WARPS
 #define GF_BWD32_WARPS 4
 #endif
+// row stride of the transposed dL/d(delta) tile: 36 floats keeps every
+// column 16-byte aligned and the lanes' 128-bit reads conflict-free
+constexpr int kGtStride = 36;
 constexpr int kBwd32Warps = GF_BWD32_WARPS;
 
 struct PairSums {
   f2 T0, U0, U1, U2, M0, M1;
 };
 
-// Sum over the 32 rows of one lane's column for one pair.
 // Backward basis with GF_CFG_BWD_EXP2: exp(q) = 2^(q * log2 e), one
 // multiply and the hardware base-2 approximation (ex2.approx.ftz).  The
 // rounding of the product costs a relative error of about |q| * 6e-8 in the
@@ -1145,63 +1147,76 @@ struct PairSums {
 // uses CUDA's expf, which the bit parity of delta requires.
 __device__ __forceinline__ float exp_via_ex2(float q) { return ex2_approx(__fmul_rn(q, kLog2e)); }
 
+// One row pair (rows 2k, 2k+1 in the two halves of R2, their dL/d(delta) in G2).
+template <bool NORM, bool TRACK_CLAMP, bool EX2>
+__device__ __forceinline__ void bwd32_row_pair(PairSums& S, f2 R2, f2 G2, f2 H00, f2 H01, f2 H11, f2 A01, f2 A11,
+                                               f2 DY, f2 MUR, float nclamp, float nf) {
+  const f2 DX = sub2(R2, MUR);
+  const f2 T1 = fma2(H00, DX, A01);
+  const f2 T2 = fma2(H01, DX, A11);
+  const f2 Q = fma2(DX, T1, mul2(DY, T2));
+  float q0, q1;
+  f2 E2 = 0;
+  if (EX2 && !TRACK_CLAMP) {
+    // base-2 basis: one packed scaling; the max(quad, 0) of the reference
+    // only removes rounding noise of order 1e-7 here (2^q = 1 + O(q))
+    E2 = ex2_2(mul2(Q, pk2(kLog2e, kLog2e)));
+  } else {
+    up2(Q, q0, q1);
+    q0 = fminf(q0, 0.0f);
+    q1 = fminf(q1, 0.0f);
+  }
+  bool act0 = true, act1 = true;
+  if (TRACK_CLAMP) {
+    act0 = q0 > nclamp;  // reference: quad < clamp
+    act1 = q1 > nclamp;
+    q0 = fmaxf(q0, nclamp);
+    q1 = fmaxf(q1, nclamp);
+  }
+  if (!(EX2 && !TRACK_CLAMP)) {
+    float e0, e1;
+    if (EX2) {
+      e0 = exp_via_ex2(q0);
+      e1 = exp_via_ex2(q1);
+    } else {
+      e0 = expf(q0);
+      e1 = expf(q1);
+    }
+    E2 = pk2(e0, e1);
+  }
+  if (NORM) E2 = mul2(E2, pk2(nf, nf));
+  const f2 GB = mul2(G2, E2);
+  if (TRACK_CLAMP) S.T0 = add2(S.T0, GB);  // without clamped elements T0 == U0 (same terms, same order)
+  f2 GBA = GB;
+  if (TRACK_CLAMP) {
+    float b0, b1;
+    up2(GB, b0, b1);
+    GBA = pk2(act0 ? b0 : 0.0f, act1 ? b1 : 0.0f);
+  }
+  S.U0 = add2(S.U0, GBA);
+  S.U1 = fma2(GBA, DX, S.U1);
+  S.U2 = fma2(mul2(GBA, DX), DX, S.U2);
+  // per-element mu factors with the reference's roundings (see render_bwd_kernel)
+  S.M0 = fma2(GBA, fma2(H01, DY, mul2(H00, DX)), S.M0);
+  S.M1 = fma2(GBA, fma2(H11, DY, mul2(H01, DX)), S.M1);
+}
+
+// Sum over the 32 rows of one lane's column for one pair: rows and the
+// column's dL/d(delta) come from shared memory four at a time (128-bit loads;
+// the row vector is a broadcast, the column is this lane's own).
 template <bool NORM, bool TRACK_CLAMP, bool EX2>
 __device__ __forceinline__ PairSums bwd32_pair_rows(const float* s_rows, const float* s_gcol, f2 H00, f2 H01,
                                                    f2 H11, f2 A01, f2 A11, f2 DY, f2 MUR, float nclamp, float nf) {
   const f2 zero2 = pk2(0.0f, 0.0f);
   PairSums S{zero2, zero2, zero2, zero2, zero2, zero2};
 #pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    const float2 rr = *reinterpret_cast<const float2*>(&s_rows[2 * k]);
-    const f2 DX = sub2(pk2(rr.x, rr.y), MUR);
-    const f2 T1 = fma2(H00, DX, A01);
-    const f2 T2 = fma2(H01, DX, A11);
-    const f2 Q = fma2(DX, T1, mul2(DY, T2));
-    float q0, q1;
-    f2 E2 = 0;
-    if (EX2 && !TRACK_CLAMP) {
-      // base-2 basis: one packed scaling; the max(quad, 0) of the reference
-      // only removes rounding noise of order 1e-7 here (2^q = 1 + O(q))
-      E2 = ex2_2(mul2(Q, pk2(kLog2e, kLog2e)));
-    } else {
-      up2(Q, q0, q1);
-      q0 = fminf(q0, 0.0f);
-      q1 = fminf(q1, 0.0f);
-    }
-    bool act0 = true, act1 = true;
-    if (TRACK_CLAMP) {
-      act0 = q0 > nclamp;  // reference: quad < clamp
-      act1 = q1 > nclamp;
-      q0 = fmaxf(q0, nclamp);
-      q1 = fmaxf(q1, nclamp);
-    }
-    if (!(EX2 && !TRACK_CLAMP)) {
-      float e0, e1;
-      if (EX2) {
-        e0 = exp_via_ex2(q0);
-        e1 = exp_via_ex2(q1);
-      } else {
-        e0 = expf(q0);
-        e1 = expf(q1);
-      }
-      E2 = pk2(e0, e1);
-    }
-    if (NORM) E2 = mul2(E2, pk2(nf, nf));
-    const float2 gg = *reinterpret_cast<const float2*>(&s_gcol[2 * k]);
-    const f2 GB = mul2(pk2(gg.x, gg.y), E2);
-    if (TRACK_CLAMP) S.T0 = add2(S.T0, GB);  // without clamped elements T0 == U0 (same terms, same order)
-    f2 GBA = GB;
-    if (TRACK_CLAMP) {
-      float b0, b1;
-      up2(GB, b0, b1);
-      GBA = pk2(act0 ? b0 : 0.0f, act1 ? b1 : 0.0f);
-    }
-    S.U0 = add2(S.U0, GBA);
-    S.U1 = fma2(GBA, DX, S.U1);
-    S.U2 = fma2(mul2(GBA, DX), DX, S.U2);
-    // per-element mu factors with the reference's roundings (see render_bwd_kernel)
-    S.M0 = fma2(GBA, fma2(H01, DY, mul2(H00, DX)), S.M0);
-    S.M1 = fma2(GBA, fma2(H11, DY, mul2(H01, DX)), S.M1);
+  for (int k = 0; k < 8; ++k) {
+    const float4 rr = *reinterpret_cast<const float4*>(&s_rows[4 * k]);
+    const float4 gg = *reinterpret_cast<const float4*>(&s_gcol[4 * k]);
+    bwd32_row_pair<NORM, TRACK_CLAMP, EX2>(S, pk2(rr.x, rr.y), pk2(gg.x, gg.y), H00, H01, H11, A01, A11, DY, MUR,
+                                           nclamp, nf);
+    bwd32_row_pair<NORM, TRACK_CLAMP, EX2>(S, pk2(rr.z, rr.w), pk2(gg.z, gg.w), H00, H01, H11, A01, A11, DY, MUR,
+                                           nclamp, nf);
   }
   if (!TRACK_CLAMP) S.T0 = S.U0;
   return S;
@@ -1211,7 +1226,7 @@ template <int NF, bool NORM, bool CLAMP, int GT, bool EX2>
 __global__ void __launch_bounds__(32 * kBwd32Warps)
 render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
   __shared__ __align__(16) float s_rows[32];
-  __shared__ __align__(16) float s_gt[32 * 34];
+  __shared__ __align__(16) float s_gt[32 * kGtStride];
   const int tg = blockIdx.x;
   const int fi = field_of_tile(p, tg);
   const DevField& F = p.f[fi];
@@ -1244,10 +1259,10 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
           const int r = q >> 3, c = (q & 7) * 4;
           const float4 v = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(F.grad) + gbase +
                                                             (size_t)r * F.in_f + c);
-          s_gt[(c + 0) * 34 + r] = v.x;
-          s_gt[(c + 1) * 34 + r] = v.y;
-          s_gt[(c + 2) * 34 + r] = v.z;
-          s_gt[(c + 3) * 34 + r] = v.w;
+          s_gt[(c + 0) * kGtStride + r] = v.x;
+          s_gt[(c + 1) * kGtStride + r] = v.y;
+          s_gt[(c + 2) * kGtStride + r] = v.z;
+          s_gt[(c + 3) * kGtStride + r] = v.w;
         }
       }
     } else {
@@ -1260,15 +1275,15 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
-          s_gt[(c + 2 * k) * 34 + r] = f.x;
-          s_gt[(c + 2 * k + 1) * 34 + r] = f.y;
+          s_gt[(c + 2 * k) * kGtStride + r] = f.x;
+          s_gt[(c + 2 * k + 1) * kGtStride + r] = f.y;
         }
       }
     }
   } else {
     for (int e = threadIdx.x; e < 1024; e += blockDim.x) {
       const int r = e >> 5, c = e & 31;
-      s_gt[c * 34 + r] =
+      s_gt[c * kGtStride + r] =
           (r < th && c < tw && GF_IN_BOUNDS((size_t)(row0 + r) * F.in_f + col0 + c < (size_t)F.out_f * F.in_f))
               ? load_grad<GT>(F.grad, (size_t)(row0 + r) * F.in_f + col0 + c)
               : 0.0f;
@@ -1285,7 +1300,7 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
   // Gaussians always take the clamp bookkeeping).
   const float corner_r = s_rows[(lane & 1) ? th - 1 : 0];
   const float corner_c = F.col[col0 + ((lane & 2) ? tw - 1 : 0)];
-  const float* s_gcol = &s_gt[lane * 34];
+  const float* s_gcol = &s_gt[lane * kGtStride];
   const int64_t* ids = ((p.batch_ids != nullptr) ? p.batch_ids : F.ids) + id_base + start;
   const float4* rec = p.records + 2 * (size_t)F.g_base;
   const int4* box = p.boxes + F.g_base;
@@ -1328,7 +1343,10 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
     const f2 H00 = pk2(h.x, h.x), H01 = pk2(h.y, h.y), A01 = pk2(a01, a01), A11 = pk2(a11, a11);
     const f2 DY = pk2(dy, dy), MUR = pk2(a.x, a.x);
     bool track = false;
-    if (CLAMP && a.w < 0.0f) {  // flagged by bwd_prep: test this tile's corners (warp-uniform)
+    // With the base-2 basis (tolerance-bound) a clamp at quad >= 64 is not
+    // tracked: a clamped element's basis is below e^-32 = 1.3e-14 of the
+    // Gaussian's peak, under the fp32 resolution of every term that matters.
+    if (CLAMP && a.w < 0.0f && !(EX2 && nclamp <= -32.0f)) {  // flagged by bwd_prep: test this tile's corners
       const bool far = corner_bound(corner_r - a.x, corner_c - a.y, h.x, h.y, h.z) > nclamp;
       track = !__all_sync(0xffffffffu, far || lane >= 4);
     }
@@ -1666,7 +1684,7 @@ cudaError_t allow_dynamic_smem(int bytes) {
 
 template <int NF>
 gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout& L, char* ws, cudaStream_t st,
-                      unsigned stages = GF_STAGE_BIN | GF_STAGE_RENDER) {
+                      unsigned stages = GF_STAGE_BIN | GF_STAGE_RENDER, int first_field = 0, int num_fields = -1) {
   // The descriptor block is large; keep one per thread instead of on the stack.
   thread_local Params<NF>* tp = nullptr;
   if (!tp) tp = new Params<NF>();
@@ -1698,7 +1716,14 @@ gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout&
   if (!(stages & GF_STAGE_BIN)) p.cfg.flags |= kFlagIdsWritten;
   NvtxRange r("gfield.render_fwd");
   const bool norm = p.cfg.normalize, clamp = p.cfg.has_clamp;
-  const int grid = (int)L.total_tiles;
+  int grid = (int)L.total_tiles;
+  if (num_fields >= 0) {  // a field range: its tiles are contiguous in the global tile order
+    const int t0 = p.f[first_field].tile_base;
+    const int t1 = first_field + num_fields < p.n ? p.f[first_field + num_fields].tile_base : (int)L.total_tiles;
+    p.tile_offset = t0;
+    grid = t1 - t0;
+    if (grid <= 0) return GF_OK;
+  }
 #define GF_FWD(N, C, O)                                                                         \
   do {                                                                                          \
     if (fast32 && O == GF_BF16 && (p.cfg.flags & GF_CFG_FWD_EXP2))                               \
@@ -1797,7 +1822,8 @@ size_t gf_workspace_bytes(const gf_config* cfg, const gf_batch* batch, gf_pass p
 }
 
 static gf_status gf_dispatch(const gf_config* cfg, const gf_batch* batch, void* workspace, size_t workspace_bytes,
-                             gf_stream stream, gf_pass pass, unsigned stages = GF_STAGE_BIN | GF_STAGE_RENDER) {
+                             gf_stream stream, gf_pass pass, unsigned stages = GF_STAGE_BIN | GF_STAGE_RENDER,
+                             int first_field = 0, int num_fields = -1) {
   gf_status s = gf::validate(cfg, batch, pass);
   if (s != GF_OK) return s;
   const gf::Layout L = gf::layout(cfg, batch, pass);
@@ -1811,9 +1837,9 @@ static gf_status gf_dispatch(const gf_config* cfg, const gf_batch* batch, void* 
   const int n = batch->num_fields;
   gf::NvtxRange r(pass == GF_PASS_FORWARD ? "gfield.forward" : "gfield.backward");
   if (pass == GF_PASS_FORWARD) {
-    if (n == 1) return gf::run_forward<1>(cfg, batch, L, ws, st, stages);
-    if (n <= 16) return gf::run_forward<16>(cfg, batch, L, ws, st, stages);
-    return gf::run_forward<GF_MAX_FIELDS>(cfg, batch, L, ws, st, stages);
+    if (n == 1) return gf::run_forward<1>(cfg, batch, L, ws, st, stages, first_field, num_fields);
+    if (n <= 16) return gf::run_forward<16>(cfg, batch, L, ws, st, stages, first_field, num_fields);
+    return gf::run_forward<GF_MAX_FIELDS>(cfg, batch, L, ws, st, stages, first_field, num_fields);
   }
   if (n == 1) return gf::run_backward<1>(cfg, batch, L, ws, st);
   if (n <= 16) return gf::run_backward<16>(cfg, batch, L, ws, st);
@@ -1830,6 +1856,16 @@ gf_status gf_forward_stages(const gf_config* cfg, const gf_batch* batch, void* w
   if (stages == 0 || (stages & ~(GF_STAGE_BIN | GF_STAGE_RENDER)))
     return gf::fail(GF_ERR_INVALID_ARG, "stages must be GF_STAGE_BIN, GF_STAGE_RENDER or both");
   return gf_dispatch(cfg, batch, workspace, workspace_bytes, stream, GF_PASS_FORWARD, stages);
+}
+
+gf_status gf_forward_render_fields(const gf_config* cfg, const gf_batch* batch, void* workspace,
+                                   size_t workspace_bytes, int32_t first_field, int32_t num_fields, gf_stream stream) {
+  if (!batch) return gf::fail(GF_ERR_INVALID_ARG, "cfg and batch must be non-null");
+  if (first_field < 0 || num_fields < 1 || first_field > batch->num_fields - num_fields)
+    return gf::fail(GF_ERR_INVALID_ARG, "field range [%d, %d) outside the batch's %d fields", first_field,
+                    first_field + num_fields, batch->num_fields);
+  return gf_dispatch(cfg, batch, workspace, workspace_bytes, stream, GF_PASS_FORWARD, GF_STAGE_RENDER, first_field,
+                     num_fields);
 }
 
 gf_status gf_backward(const gf_config* cfg, const gf_batch* batch, void* workspace, size_t workspace_bytes,

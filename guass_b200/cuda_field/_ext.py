@@ -125,12 +125,13 @@ def _ptr(t) -> int | None:
     return t.data_ptr() if t is not None else None
 
 
-def raise_device_flags(ws: torch.Tensor) -> None:
-    """Synchronise and raise if the device recorded an error condition."""
+def raise_device_flags(ws: torch.Tensor, ignore: int = 0) -> None:
+    """Synchronise and raise if the device recorded an error condition
+    (other than the bits in ``ignore``)."""
     flags = ctypes.c_uint32(0)
     stream = torch.cuda.current_stream(ws.device).cuda_stream
     _lib.check(_lib.lib().gf_workspace_status(ws.data_ptr(), stream, 1, ctypes.byref(flags)))
-    f = flags.value
+    f = flags.value & ~ignore
     if f & _lib.GF_FLAG_STATE:
         raise RuntimeError("saved tile_ptr / gaussian_ids_sorted do not match mu and chol_raw "
                            "(out-of-range, unsorted or foreign pair)")
@@ -140,12 +141,23 @@ def raise_device_flags(ws: torch.Tensor) -> None:
         raise RuntimeError("internal error: per-tile Gaussian list disagreed with tile_ptr")
 
 
+class _PairProbe:
+    """The training forward's pair count on its way to the host: a pinned
+    one-element tensor, the event after its copy, the id capacity used."""
+
+    __slots__ = ("count", "done", "capacity")
+
+    def __init__(self, count, done, capacity):
+        self.count, self.done, self.capacity = count, done, capacity
+
+
 class GaussianFieldExtension:
     """Drop-in for the reference's extension module (ext.cpp:9-110)."""
 
     def __init__(self):
         self._lib = _lib.lib()
         self._pairs_hint: dict[tuple, int] = {}
+        self._train_hint: dict[tuple, int] = {}
 
     # ext.cpp:9-37, field_impl.cu:135-163
     def gaussian_field_forward(self, row_coords, col_coords, mu, chol_raw, amp, tile_out, tile_in,
@@ -255,17 +267,28 @@ class GaussianFieldExtension:
                 raise_device_flags(ws)
         return [d_mu, d_chol, d_amp]
 
-    # Training path without host round trips.  The public forward must return
-    # gaussian_ids_sorted with exactly num_pairs entries, which costs one
-    # host read of the pair count per layer (the reference makes the same
-    # read, forward.cu:48-73).  The autograd training function only returns
-    # delta, so it can keep the binning in the library's shared-id form: ids
-    # in a buffer sized for the exact bound (every Gaussian in every tile --
-    # no overflow, no retry) and the pair count on the device (pair_base).
-    # Neither pass then reads anything back.  Same kernels and per-pair slot
-    # order as the public path, so the same delta and gradients.
+    # Training path without host round trips in steady state.  The public
+    # forward must return gaussian_ids_sorted with exactly num_pairs entries,
+    # which costs one host read of the pair count per layer (the reference
+    # makes the same read, forward.cu:48-73).  The autograd training function
+    # only returns delta, so it keeps the binning in the library's shared-id
+    # form with the pair count on the device (pair_base) and copies that count
+    # to pinned host memory asynchronously.  The id buffer is sized from the
+    # previous call of the same layer shape (+25 %; every Gaussian in every
+    # tile is the bound, K*T ids, which for a densified layer is hundreds of
+    # MB), the backward's pair partials from this call's count, read when the
+    # backward runs (long after the copy completed).  If the count outgrew the
+    # id buffer (first call, or a layer whose Gaussians grew), the backward
+    # bins again with room before it reads the ids: the forward's delta never
+    # depends on the id buffer, so it is right either way.
+    _HINT_SLACK = 4096
+
+    @staticmethod
+    def _train_key(device, out_f, in_f, k, tile_out, tile_in, sigma_multiplier):
+        return (device.index, out_f, in_f, k, int(tile_out), int(tile_in), float(sigma_multiplier))
+
     def train_forward(self, row_coords, col_coords, mu, chol_raw, amp, tile_out, tile_in, sigma_multiplier,
-                      normalize, clamp_quad):
+                      normalize, clamp_quad, capacity=None):
         _validate_forward_inputs(row_coords, col_coords, mu, chol_raw, amp)
         _check_config(tile_out, tile_in, sigma_multiplier)
         device = mu.device
@@ -274,8 +297,12 @@ class GaussianFieldExtension:
         delta = torch.empty(out_f * in_f, dtype=torch.float32, device=device)
         tile_ptr = torch.empty(num_tiles + 1, dtype=torch.int64, device=device)
         pair_base = torch.zeros(2, dtype=torch.int64, device=device)
-        cap = k * num_tiles
-        ids = torch.empty(max(cap, 1), dtype=torch.int64, device=device)
+        bound = k * num_tiles
+        if capacity is None:
+            hint = self._train_hint.get(self._train_key(device, out_f, in_f, k, tile_out, tile_in, sigma_multiplier))
+            capacity = hint + hint // 4 + self._HINT_SLACK if hint is not None else 64 * k + self._HINT_SLACK
+        cap = max(1, min(bound, int(capacity)))
+        ids = torch.empty(cap, dtype=torch.int64, device=device)
         cfg = make_config(tile_out, tile_in, sigma_multiplier, normalize, clamp_quad)
         field = _lib.GfField(out_features=out_f, in_features=in_f, num_gaussians=k,
                              row_coords=row_coords.data_ptr(), col_coords=col_coords.data_ptr(),
@@ -288,15 +315,20 @@ class GaussianFieldExtension:
             _lib.check(_lib.GF_ERR_INVALID_ARG)
         with torch.cuda.device(device):
             ws = _POOL.get(device, nbytes)
-            stream = torch.cuda.current_stream(device).cuda_stream
+            stream = torch.cuda.current_stream(device)
             _lib.check(self._lib.gf_forward(ctypes.byref(cfg), ctypes.byref(batch), ws.data_ptr(), ws.numel(),
-                                            stream))
+                                            stream.cuda_stream))
+            count = torch.empty(1, dtype=torch.int64, pin_memory=True)
+            count.copy_(pair_base[1:], non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(stream)
             if _VALIDATE:
-                raise_device_flags(ws)
-        return delta, tile_ptr, ids, pair_base
+                raise_device_flags(ws, ignore=_lib.GF_FLAG_CAPACITY)
+        probe = _PairProbe(count, done, cap)
+        return delta, tile_ptr, ids, pair_base, probe
 
     def train_backward(self, grad_delta, row_coords, col_coords, mu, chol_raw, amp, tile_ptr, ids, pair_base,
-                       tile_out, tile_in, sigma_multiplier, normalize, clamp_quad):
+                       tile_out, tile_in, sigma_multiplier, normalize, clamp_quad, probe=None):
         _check_cuda(grad_delta, "grad_delta")
         if grad_delta.dtype not in (torch.float32, torch.bfloat16):
             raise RuntimeError("grad_delta must be float32")
@@ -309,6 +341,17 @@ class GaussianFieldExtension:
         d_amp = torch.empty(k, 1, dtype=torch.float32, device=device)
         if k == 0:
             return [d_mu, d_chol, d_amp]
+        n_pairs = ids.numel()
+        if probe is not None:
+            probe.done.synchronize()
+            n_pairs = int(probe.count[0])
+            self._train_hint[self._train_key(device, out_f, in_f, k, tile_out, tile_in, sigma_multiplier)] = n_pairs
+            if len(self._train_hint) > 4096:
+                self._train_hint.pop(next(iter(self._train_hint)))
+            if n_pairs > probe.capacity:  # the forward's id buffer overflowed: bin again with room
+                _, tile_ptr, ids, pair_base, _ = self.train_forward(row_coords, col_coords, mu, chol_raw, amp,
+                                                                    tile_out, tile_in, sigma_multiplier, normalize,
+                                                                    clamp_quad, capacity=n_pairs)
         gdt = _lib.GF_BF16 if grad_delta.dtype == torch.bfloat16 else _lib.GF_F32
         cfg = make_config(tile_out, tile_in, sigma_multiplier, normalize, clamp_quad, grad_dtype=gdt)
         field = _lib.GfField(out_features=out_f, in_features=in_f, num_gaussians=k,
@@ -316,8 +359,9 @@ class GaussianFieldExtension:
                              mu=mu.data_ptr(), chol_raw=chol_raw.data_ptr(), amp=amp.data_ptr(),
                              tile_ptr=tile_ptr.data_ptr(), grad_delta=grad_delta.data_ptr(), d_mu=d_mu.data_ptr(),
                              d_chol_raw=d_chol.data_ptr(), d_amp=d_amp.data_ptr())
+        # partial slots for exactly this call's pairs (the id buffer may be larger)
         batch = _lib.GfBatch(num_fields=1, fields=ctypes.pointer(field), ids=ids.data_ptr(),
-                             ids_capacity=ids.numel(), pair_base=pair_base.data_ptr())
+                             ids_capacity=max(1, min(n_pairs, ids.numel())), pair_base=pair_base.data_ptr())
         nbytes = self._lib.gf_workspace_bytes(ctypes.byref(cfg), ctypes.byref(batch), _lib.GF_PASS_BACKWARD)
         if nbytes == 0:
             _lib.check(_lib.GF_ERR_INVALID_ARG)

@@ -48,10 +48,10 @@ class GaussianFieldCudaTrainFunction(_FieldFunctionBase):
 
     With this package's extension the binning stays in the library's
     shared-id form (``train_forward`` / ``train_backward``): the same kernels
-    and results, but no host read of the pair count per call, so a model's
-    layers render without a synchronisation each.  The saved state is then the
-    reference's seven tensors with the id buffer at its bound and the device
-    pair count appended.  Any other extension object (e.g. the reference's
+    and results, but the pair count travels to the host asynchronously, so a
+    model's layers render without a synchronisation each.  The saved state is
+    then the reference's seven tensors with the device pair count appended
+    (and its host copy on the context).  Any other extension object (e.g. the reference's
     own) is driven through the reference protocol."""
 
     @staticmethod
@@ -66,8 +66,9 @@ class GaussianFieldCudaTrainFunction(_FieldFunctionBase):
                                                               tile_in, sigma_multiplier, normalize, clamp_quad)
             ctx.save_for_backward(row_coords, col_coords, mu, chol_raw, amp, tile_ptr, ids)
             return delta
-        delta, tile_ptr, ids, pair_base = ext.train_forward(row_coords, col_coords, mu, chol_raw, amp, tile_out,
-                                                            tile_in, sigma_multiplier, normalize, clamp_quad)
+        delta, tile_ptr, ids, pair_base, ctx.probe = ext.train_forward(row_coords, col_coords, mu, chol_raw, amp,
+                                                                       tile_out, tile_in, sigma_multiplier, normalize,
+                                                                       clamp_quad)
         ctx.save_for_backward(row_coords, col_coords, mu, chol_raw, amp, tile_ptr, ids, pair_base)
         return delta
 
@@ -76,7 +77,8 @@ class GaussianFieldCudaTrainFunction(_FieldFunctionBase):
         if not ctx.shared_ids:
             return GaussianFieldCudaTrainFunction._backward(ctx, grad_delta)
         ext = load_extension(verbose=False)
-        d_mu, d_chol_raw, d_amp = ext.train_backward(grad_delta.contiguous(), *ctx.saved_tensors, *ctx.field_args)
+        d_mu, d_chol_raw, d_amp = ext.train_backward(grad_delta.contiguous(), *ctx.saved_tensors, *ctx.field_args,
+                                                     probe=ctx.probe)
         return None, None, d_mu, d_chol_raw, d_amp, None, None, None, None, None
 
 

@@ -229,23 +229,36 @@ class PartitionedRenderer:
         self.fused = bool(fused) and self.symm is not None
         self.exchange = ("nvls-multicast-fused-render" if self.fused else "nvls-multicast") if self.symm is not None \
             else ("nccl-all-gather" if world > 1 else "none")
-        # one FieldBatch per non-empty group of this rank; parameters and
-        # gradients stay packed in ``own`` order (groups are runs of it)
-        self.batches, self.batch_group, self.k_off, self.n_off = [], [], [0], [0]
-        by_field = {f: (int(shapes[f][0]), int(shapes[f][1]), int(shapes[f][2])) for f in self.own}
+        # One FieldBatch over all of this rank's fields (parameters and
+        # gradients packed in ``own`` order): one binning and one backward per
+        # step; the forward renders group by group (gf_forward_render_fields)
+        # into the fields' places in the gather buffer.
+        by_field = [(int(shapes[f][0]), int(shapes[f][1]), int(shapes[f][2])) for f in self.own]
+        self.k_own = [0]
+        for sh in by_field:
+            self.k_own.append(self.k_own[-1] + sh[2])
+        self.n_own = [0]
+        for f in self.own:
+            self.n_own.append(self.n_own[-1] + numels[f])
+        # field ranges (indices into ``own``) of this rank's non-empty groups, with their group index
+        self.ranges = []
+        pos = 0
         for g, run in enumerate(self.layout.rank_groups[rank]):
-            if not run:
-                continue
-            n0, n1 = self.n_off[-1], self.n_off[-1] + sum(numels[f] for f in run)
-            dst = self.layout.chunk(self.gathered, g, rank)[:n1 - n0]
-            mc = None
+            if run:
+                self.ranges.append((g, pos, len(run)))
+                pos += len(run)
+        self.batches = []
+        if self.own:
             if self.fused:
+                g = self.ranges[0][0]
+                dst = self.layout.chunk(self.gathered, g, rank)[:self.n_own[-1]]
                 mc = self.mc_ptr + (self.layout.base[g] + rank * self.layout.slot[g]) * self.gathered.element_size()
-            self.batches.append(FieldBatch([by_field[f] for f in run], out_dtype=out_dtype, device=dev,
-                                           delta_out=dst, delta_multicast=mc, **batch_kw))
-            self.batch_group.append(g)
-            self.n_off.append(n1)
-            self.k_off.append(self.k_off[-1] + sum(by_field[f][2] for f in run))
+                self.batches.append(FieldBatch(by_field, out_dtype=out_dtype, device=dev, delta_out=dst,
+                                               delta_multicast=mc, **batch_kw))
+            else:
+                outs = [self.layout.field_view(self.gathered, f) for f in self.own]
+                self.batches.append(FieldBatch(by_field, out_dtype=out_dtype, device=dev, field_outputs=outs,
+                                               **batch_kw))
         self.side = torch.cuda.Stream(device=dev) if world > 1 else None
         self.gather_events = None  # optional list of (start, end) event pairs to record into
         self.graph = None
@@ -256,19 +269,14 @@ class PartitionedRenderer:
 
     def field_grads(self, f: int, outs):
         """(d_mu, d_chol_raw, d_amp) of own field ``f`` from :meth:`step`'s result."""
-        g = self.layout.group_of[f]
-        i = self.batch_group.index(g)
-        run = self.layout.rank_groups[self.rank][g]
-        k_field = self.batches[i].shapes
-        k0 = sum(k_field[j].num_gaussians for j in range(run.index(f)))
-        k = k_field[run.index(f)].num_gaussians
-        return tuple(t[k0:k0 + k] for t in outs[i])
+        j = self.own.index(f)
+        k0, k1 = self.k_own[j], self.k_own[j + 1]
+        return tuple(t[k0:k1] for t in outs[0])
 
     def ensure_capacity(self, mu, chol_raw, amp):
         grew = False
-        for i, b in enumerate(self.batches):
-            k0, k1 = self.k_off[i], self.k_off[i + 1]
-            while b.ensure_capacity(mu[k0:k1], chol_raw[k0:k1], amp[k0:k1]):
+        for b in self.batches:
+            while b.ensure_capacity(mu, chol_raw, amp):
                 grew = True
         return grew
 
@@ -317,46 +325,68 @@ class PartitionedRenderer:
 
     def step(self, mu, chol_raw, amp, grad):
         """Forward + exchange + backward for this rank's packed parameters
-        (fields in ``own`` order); returns the packed gradients."""
+        (fields in ``own`` order); returns [packed gradients]."""
+        from guass_b200 import _lib
+
         if self.fused:
             return self._step_fused(mu, chol_raw, amp, grad)
         main = torch.cuda.current_stream(self.device)
+        b = self.batches[0] if self.batches else None
+        if self.world == 1:
+            b.forward(mu, chol_raw, amp)
+            return [b.backward(grad, mu, chol_raw, amp)]
         ev = None
-        if self.world > 1 and self.gather_events is not None:
+        if self.gather_events is not None:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        if b is not None:
+            b.forward_stages(mu, chol_raw, amp, _lib.GF_STAGE_BIN, main)
         nxt = 0  # next group to exchange (every rank exchanges every group, in order)
-        for i, b in enumerate(self.batches):
-            k0, k1 = self.k_off[i], self.k_off[i + 1]
-            b.forward(mu[k0:k1], chol_raw[k0:k1], amp[k0:k1])
-            if self.world > 1:
-                self.side.wait_stream(main)
-                with torch.cuda.stream(self.side):
-                    if nxt == 0 and ev is not None:
-                        ev[0].record()
-                    while nxt <= self.batch_group[i]:
-                        self._exchange_group(nxt)
-                        nxt += 1
-        if self.world > 1:
+        for g, first, count in self.ranges:
+            b.forward_render_fields(mu, chol_raw, amp, first, count, main)
             self.side.wait_stream(main)
             with torch.cuda.stream(self.side):
                 if nxt == 0 and ev is not None:
                     ev[0].record()
-                while nxt < self.layout.num_groups:
+                while nxt <= g:
                     self._exchange_group(nxt)
                     nxt += 1
-                if self.symm is not None:
-                    self.symm.barrier()
-                if ev is not None:
-                    ev[1].record()
-                    self.gather_events.append(ev)
-        outs = []
-        for i, b in enumerate(self.batches):
-            k0, k1 = self.k_off[i], self.k_off[i + 1]
-            n0, n1 = self.n_off[i], self.n_off[i + 1]
-            outs.append(b.backward(grad[n0:n1], mu[k0:k1], chol_raw[k0:k1], amp[k0:k1]))
-        if self.world > 1:
-            main.wait_stream(self.side)
+        self.side.wait_stream(main)
+        with torch.cuda.stream(self.side):
+            if nxt == 0 and ev is not None:
+                ev[0].record()
+            while nxt < self.layout.num_groups:
+                self._exchange_group(nxt)
+                nxt += 1
+            if self.symm is not None:
+                self.symm.barrier()
+            if ev is not None:
+                ev[1].record()
+                self.gather_events.append(ev)
+        outs = [b.backward(grad, mu, chol_raw, amp)] if b is not None else []
+        main.wait_stream(self.side)
         return outs
+
+    def kernel_times(self, ev) -> dict:
+        """Per-kernel times (ms) of one step from its library trace events
+        (gf_trace_events, in host call order; see :meth:`trace_events_per_step`)."""
+        if self.fused:
+            # BIN stage (start, bin), backward on the side stream (start, prep, render,
+            # finalize), RENDER stage (render: from the end of binning, overlapping the backward)
+            return {"bin": ev[0].elapsed_time(ev[1]), "render_fwd": ev[1].elapsed_time(ev[6]),
+                    "bwd_prep": ev[2].elapsed_time(ev[3]), "render_bwd": ev[3].elapsed_time(ev[4]),
+                    "bwd_finalize": ev[4].elapsed_time(ev[5])}
+        nf = 3 if self.world == 1 else 2 + len(self.ranges)  # start, bin, renders
+        b = ev[nf:]
+        return {"bin": ev[0].elapsed_time(ev[1]), "render_fwd": ev[1].elapsed_time(ev[nf - 1]),
+                "bwd_prep": b[0].elapsed_time(b[1]), "render_bwd": b[1].elapsed_time(b[2]),
+                "bwd_finalize": b[2].elapsed_time(b[3])}
+
+    def trace_events_per_step(self) -> int:
+        if not self.batches:
+            return 0
+        if self.fused:
+            return 7
+        return (3 if self.world == 1 else 2 + len(self.ranges)) + 4
 
     def capture(self, mu, chol_raw, amp, grad, warmup: int = 2):
         """Record one :meth:`step` on these tensors into a CUDA graph.
@@ -372,6 +402,8 @@ class PartitionedRenderer:
         if self.world > 1 and self.symm is None:
             raise RuntimeError("capture() supports the multicast exchange or a single rank; "
                                "run step() eagerly with the NCCL exchange")
+        for b in self.batches:
+            b.reserve_backward_workspace()
         cur = torch.cuda.current_stream(self.device)
         warm = torch.cuda.Stream(device=self.device)
         warm.wait_stream(cur)

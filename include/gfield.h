@@ -206,6 +206,18 @@ int gf_trace_count(void);
 gf_status gf_forward_stages(const gf_config* cfg, const gf_batch* batch, void* workspace, size_t workspace_bytes,
                             unsigned stages, gf_stream stream);
 
+/* The RENDER stage of gf_forward_stages for the fields [first_field,
+ * first_field + num_fields) of the batch only (no reference counterpart: the
+ * reference renders one layer per call).  It must follow a BIN stage of the
+ * same batch, parameters and workspace in stream order; disjoint ranges may
+ * be rendered by separate calls, so that work on one range's delta (an
+ * exchange to other GPUs) starts while the next range renders.  The batch
+ * descriptors are those of the BIN stage; only the range's delta is written.
+ * Trace events: 1 (render). */
+gf_status gf_forward_render_fields(const gf_config* cfg, const gf_batch* batch, void* workspace,
+                                   size_t workspace_bytes, int32_t first_field, int32_t num_fields,
+                                   gf_stream stream);
+
 /* Multi-GPU publish (no reference counterpart; GUASS has no layer
  * partitioning).  Copies `bytes` from the local device buffer `src` to
  * `mc_dst`, an NVLink multicast (NVLS) address of a buffer that every GPU of

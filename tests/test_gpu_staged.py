@@ -60,3 +60,46 @@ def test_backward_overlapping_the_render_matches_the_sequence():
         for g, w in zip(got, want):
             assert torch.equal(g, w)
     assert b.device_flags() == 0
+
+
+def test_field_range_renders_equal_the_full_forward():
+    """BIN once, then gf_forward_render_fields over disjoint ranges (the
+    multi-GPU schedule) into per-field outputs scattered in a larger buffer:
+    every field's delta equals the full forward's bit for bit, and the
+    untouched gaps keep their fill."""
+    shapes, (mu, chol, amp, grad), cap = _setup()
+    a = FieldBatch(shapes, ids_capacity=cap)
+    want = a.forward(mu, chol, amp).clone()
+    numels = [o * i for o, i, _ in shapes]
+    gap = 64
+    buf = torch.full((sum(numels) + gap * len(shapes),), 7.0, dtype=torch.bfloat16, device="cuda")
+    outs, off = [], 0
+    for n in numels:
+        off += gap
+        outs.append(buf[off:off + n])
+        off += n
+    b = FieldBatch(shapes, ids_capacity=cap, field_outputs=outs)
+    b.forward_stages(mu, chol, amp, _lib.GF_STAGE_BIN)
+    for first, count in ((0, 5), (5, 1), (6, 11), (17, 7)):
+        b.forward_render_fields(mu, chol, amp, first, count)
+    torch.cuda.synchronize()
+    for f in range(len(shapes)):
+        assert torch.equal(b.delta_view(f).reshape(-1), want[a.n_off[f]:a.n_off[f + 1]]), f
+    off = 0
+    for n in numels:
+        assert bool((buf[off:off + gap] == 7.0).all())
+        off += gap + n
+    got = b.backward(grad, mu, chol, amp)
+    ref = a.backward(grad, mu, chol, amp)
+    for g, r in zip(got, ref):
+        assert torch.equal(g, r)
+    assert a.device_flags() == 0 and b.device_flags() == 0
+
+
+def test_field_range_arguments_are_checked():
+    shapes, (mu, chol, amp, grad), cap = _setup()
+    b = FieldBatch(shapes, ids_capacity=cap)
+    b.forward_stages(mu, chol, amp, _lib.GF_STAGE_BIN)
+    for first, count in ((-1, 2), (0, 0), (20, 5)):
+        with pytest.raises(_lib.GfieldError, match="field range"):
+            b.forward_render_fields(mu, chol, amp, first, count)
