@@ -81,6 +81,8 @@ def parse_args():
                     "reference-extension timings (N=1)")
     ap.add_argument("--fields", type=int, default=128,
                     help="cfg3 slice for profiling: this many of the 128 fields, spread over the UNet's widths")
+    ap.add_argument("--profile-field", choices=["cfg1", "cfg2", "dense4096", "dense16384"], default=None,
+                    help="with --profile-case: one field of that configuration instead of the cfg3 slice")
     ap.add_argument("--profile-case", action="store_true",
                     help="only run warm-up + steps of the workload eagerly and exit (the command that the ncu "
                          "summaries under profiles/ capture)")
@@ -329,39 +331,62 @@ def run_e2e_batched(w: UNetWorkload, steps: int, warmup: int, world: int):
     return ms, sum_over_ranks(h2d, world), sum_over_ranks(d2h, world)
 
 
-def run_e2e(w: UNetWorkload, steps: int, warmup: int, world: int):
-    """The same step through the drop-in per-layer API with host buffers: per
-    layer, ``gaussian_field_train`` (what GaussianLinear calls in
-    cuda_field_train mode, gaussian_linear.py:178-190) forward, then its
-    autograd backward."""
-    from guass_b200 import cuda_field
-    from guass_b200.partition import all_gather_slots
+def run_e2e_model(w: UNetWorkload, steps: int, warmup: int, world: int, mode: str):
+    """The same step through GUASS's layer API: a model of this rank's
+    projection layers (GaussianLinear's interface, guass_b200.sd15.
+    GaussianProjection, with this workload's shapes and K), whose forward asks
+    every layer for ``compute_delta_weight()`` as GaussianLinear.forward does
+    (gaussian_linear.py:162-242), then one autograd backward with each layer's
+    dL/d(delta).  ``mode`` "dropin": every layer renders itself through the
+    drop-in runtime (gaussian_field_train, the reference's call pattern);
+    "model_renderer": adapters.ModelRenderer serves every layer from one
+    batched render per model forward.  Every step copies the layers'
+    parameters and dL/d(delta) from pinned host memory and the parameter
+    gradients back; the model runs all layer forwards before the backward."""
+    from torch import nn
 
-    host = []
-    for i in w.own:
+    from guass_b200 import sd15
+    from guass_b200.adapters import ModelRenderer
+
+    settings = sd15.AdapterSettings()
+    layers = nn.ModuleList()
+    for n, i in enumerate(w.own):
         f = w.fields[i]
-        host.append(dict(mu=f.mu.pin_memory(), chol=f.chol_raw.pin_memory(), amp=f.amp.pin_memory(),
-                         grad=f.grad.pin_memory(), row=f.row_coords.cuda(), col=f.col_coords.cuda(),
-                         out=[torch.empty_like(f.mu).pin_memory(), torch.empty_like(f.chol_raw).pin_memory(),
-                              torch.empty_like(f.amp).pin_memory()]))
-    h2d = sum(sum(h[k].numel() * h[k].element_size() for k in ("mu", "chol", "amp", "grad")) for h in host)
-    d2h = sum(sum(o.numel() * o.element_size() for o in h["out"]) for h in host)
+        layers.append(sd15.GaussianProjection(f.in_features, f.out_features, False, f.k, seed=i,
+                                              dtype=torch.bfloat16, settings=settings))
+
+    class DeltaModel(nn.Module):
+        def __init__(self, layers):
+            super().__init__()
+            self.layers = layers
+
+        def forward(self):
+            return [m.compute_delta_weight() for m in self.layers]
+
+    model = DeltaModel(layers).cuda()
+    if mode == "dropin":
+        sd15.PerLayerRender({str(n): m for n, m in enumerate(layers)}).install()
+    else:
+        ModelRenderer(model, out_dtype=torch.bfloat16)
+    params = [p for m in layers for p in (m.mu_raw, m.chol_raw, m.amp)]
+    h_params = [p.detach().cpu().pin_memory() for p in params]
+    h_grads = [w.fields[i].grad.view(w.fields[i].out_features, w.fields[i].in_features).pin_memory() for i in w.own]
+    d_grads = [g.cuda() for g in h_grads]
+    h_out = [torch.empty(p.shape, dtype=p.dtype).pin_memory() for p in params]
+    h2d = sum(t.numel() * t.element_size() for t in h_params + h_grads)
+    d2h = sum(t.numel() * t.element_size() for t in h_out)
 
     def step():
-        for i, h in zip(w.own, host):
-            mu = h["mu"].to("cuda", non_blocking=True).requires_grad_(True)
-            chol = h["chol"].to("cuda", non_blocking=True).requires_grad_(True)
-            amp = h["amp"].to("cuda", non_blocking=True).requires_grad_(True)
-            delta = cuda_field.gaussian_field_train(row_coords=h["row"], col_coords=h["col"], mu=mu, chol_raw=chol,
-                                                    amp=amp, tile_out=32, tile_in=32, sigma_multiplier=3.0,
-                                                    normalize=False, clamp_quad=80.0)
-            w.layout.field_view(w.gathered, i).copy_(delta.detach())  # the layer's bf16 weight dtype cast
-            g = h["grad"].to("cuda", non_blocking=True)
-            delta.backward(g)
-            for o, p in zip(h["out"], (mu, chol, amp)):
-                o.copy_(p.grad, non_blocking=True)
-        if world > 1:
-            all_gather_slots(w.gathered, w.layout, w.rank)
+        with torch.no_grad():
+            for p, h in zip(params, h_params):
+                p.copy_(h, non_blocking=True)
+            for d, h in zip(d_grads, h_grads):
+                d.copy_(h, non_blocking=True)
+        deltas = model()
+        torch.autograd.backward(deltas, [g.to(d.dtype) for d, g in zip(deltas, d_grads)])
+        for p, h in zip(params, h_out):
+            h.copy_(p.grad, non_blocking=True)
+            p.grad = None
 
     for _ in range(warmup):
         step()
@@ -613,6 +638,58 @@ def time_reference_cuda(fields, out_bf16: bool, steps: int, warmup: int):
     return start.elapsed_time(end) / steps
 
 
+def time_dropin_train(f, steps: int, warmup: int):
+    """The drop-in training call GUASS's layers make (gaussian_field_train,
+    fp32 delta, its autograd backward) on one field: ms per forward+backward
+    and the peak device memory it adds."""
+    from guass_b200 import cuda_field
+
+    d = f.to("cuda")
+    mu, chol, amp = (t.clone().requires_grad_(True) for t in (d.mu, d.chol_raw, d.amp))
+
+    def step():
+        delta = cuda_field.gaussian_field_train(row_coords=d.row_coords, col_coords=d.col_coords, mu=mu,
+                                                chol_raw=chol, amp=amp, tile_out=32, tile_in=32, sigma_multiplier=3.0)
+        delta.backward(d.grad)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats()
+    base = torch.cuda.memory_allocated()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / steps, torch.cuda.max_memory_allocated() - base
+
+
+def dense_rows(a, ns_per_eval_fwd: float):
+    """Densified layers (1280x1280, K = 4096 and 16384): the per-tile candidate
+    scan reads all K boxes per tile, so its cost grows with K x tiles while the
+    render work grows with the pairs.  Each row compares the forward render
+    with that work at the whole-UNet rate per evaluation (the scan's excess)."""
+    from guass_b200 import synthetic
+
+    rows = {}
+    for k in (4096, 16384):
+        f = synthetic.densified(k)
+        ms, kern, evals = time_single_field(f, a.fwd_exp == "ex2", a.bwd_exp == "ex2", torch.bfloat16, 20, 3)
+        work_ms = evals * ns_per_eval_fwd * 1e-6
+        t_ms, peak = time_dropin_train(f, 5, 2)
+        rows[f"dense{k}"] = {
+            "workload": f"1280x1280 field, K={k} (densified: log s ~ N(log(0.02*sqrt(1024/K)), 0.3)), bf16 delta",
+            "ms_per_step": ms, "value": f.numel / (ms / 1e3), "unit": "elements/s", "evals": evals,
+            "kernels_ms": kern, "render_fwd_at_unet_rate_ms": work_ms,
+            "scan_excess_share": max(0.0, kern["render_fwd"] - work_ms) / kern["render_fwd"],
+            "dropin_train": {"ms_per_step": t_ms, "peak_bytes": peak,
+                             "k_times_tiles_bound_bytes": 40 * k * 1600,
+                             "path": "cuda_field.gaussian_field_train + autograd backward, fp32 delta"}}
+    return rows
+
+
 def single_field_configs(a, f_mhz, sm_count):
     """BASELINE configs 1 and 2 at N=1: one field each, forward + backward."""
     from guass_b200 import synthetic
@@ -825,6 +902,24 @@ def main():
         return
     rank, world, local = setup_dist()
     fx, bx = a.fwd_exp == "ex2", a.bwd_exp == "ex2"
+    if a.profile_case and a.profile_field:
+        from guass_b200 import synthetic
+        from guass_b200.batched import FieldBatch, pack_fields
+
+        name = a.profile_field
+        f = synthetic.densified(int(name[5:])) if name.startswith("dense") else synthetic.CONFIGS[name]()
+        out_dtype = torch.float32 if name == "cfg2" else torch.bfloat16
+        b = FieldBatch([(f.out_features, f.in_features, f.k)], out_dtype=out_dtype, fwd_exp2=fx, bwd_exp2=bx)
+        mu, chol, amp, grad = pack_fields([f], device="cuda")
+        while b.ensure_capacity(mu, chol, amp):
+            pass
+        for _ in range(a.warmup + a.steps):
+            b.forward(mu, chol, amp)
+            b.backward(grad, mu, chol, amp)
+        torch.cuda.synchronize()
+        print(f"profile case: {name}, {f.numel} elements, {b.total_pairs()} pairs, {a.warmup + a.steps} steps",
+              flush=True)
+        return
     w = UNetWorkload(rank, world, a.exchange, a.groups, bwd_exp2=bx, fwd_exp2=fx, num_fields=a.fields)
     if a.profile_case:
         for _ in range(a.warmup + a.steps):
@@ -880,15 +975,22 @@ def main():
                            "step's inputs copy on a second stream while this step computes"}
         except Exception as exc:  # report, do not lose the device-timed line
             e2e = {"error": f"{type(exc).__name__}: {exc}"}
-        try:
-            e2e_ms, h2d, d2h = run_e2e(w, n_e2e, 2, world)
-            e2e_layer = {"value": w.total_elements / (e2e_ms / 1e3), "unit": UNIT, "ms_per_step": e2e_ms,
-                         "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-                         "path": "guass_b200.cuda_field.gaussian_field_train per layer with its autograd backward "
-                                 "(what GaussianLinear calls; 128 renders, fp32 delta, binning kept on the device), "
-                                 "pinned host params/grads"}
-        except Exception as exc:
-            e2e_layer = {"error": f"{type(exc).__name__}: {exc}"}
+        e2e_layer = {}
+        for mode, key in ((("dropin", "e2e_dropin_per_layer"), ("model_renderer", "e2e_model_renderer"))
+                          if world == 1 else ()):
+            try:
+                e2e_ms, h2d, d2h = run_e2e_model(w, n_e2e, 2, world, mode)
+                e2e_layer[key] = {
+                    "value": w.total_elements / (e2e_ms / 1e3), "unit": UNIT, "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                    "path": ("GUASS layer API: every layer's compute_delta_weight() through "
+                             "guass_b200.cuda_field.gaussian_field_train (one render per layer, the reference's call "
+                             "pattern), fp32 delta" if mode == "dropin" else
+                             "GUASS layer API with adapters.ModelRenderer: one batched render per model forward "
+                             "(bf16 delta), one batched backward") +
+                            "; layer params and dL/d(delta) H2D from pinned memory, gradients D2H, every step"}
+            except Exception as exc:  # noqa: BLE001
+                e2e_layer[key] = {"error": f"{type(exc).__name__}: {exc}"}
 
     sm_count = torch.cuda.get_device_properties(0).multi_processor_count
     f_mhz = (clocks or {}).get("sm_mhz") or 1965.0
@@ -901,6 +1003,10 @@ def main():
             except Exception as exc:  # noqa: BLE001
                 extra["configs"] = {"error": f"{type(exc).__name__}: {exc}"}
             ref_ms = time_reference_cuda(w.fields, True, 2, 1)
+            try:
+                extra["dense"] = dense_rows(a, kern_max["render_fwd"] / w.total_evals * 1e6)
+            except Exception as exc:  # noqa: BLE001
+                extra["dense"] = {"error": f"{type(exc).__name__}: {exc}"}
             if ref_ms is not None:
                 extra["ref_cuda"] = {"ms_per_step": ref_ms, "value": w.total_elements / (ref_ms / 1e3),
                                      "speedup": ref_ms / ms,
@@ -953,13 +1059,14 @@ def main():
         "reference_basis": ref_basis,
         "clocks": clocks,
         "e2e": e2e,
-        "e2e_dropin_per_layer": e2e_layer,
+        **(e2e_layer or {}),
         "cpu_baseline": cpu,
         **extra,
-        # per step: bin (+ the id lists when the render runs in field groups), one render per group,
-        # prep, backward render, finalize, (+ one publish kernel per group of the multicast exchange)
+        # per step: bin (+ the id lists when the render runs in field groups), per render call the
+        # regular and the heavy-tile kernel, prep, backward render (regular + heavy), finalize
+        # (+ one publish kernel per group of the multicast exchange)
         "gpu_launches": a.steps * world * (
-            5 if world == 1 else (2 + (1 if w.renderer.fused else len(w.renderer.ranges)) + 3
+            7 if world == 1 else (2 + 2 * (1 if w.renderer.fused else len(w.renderer.ranges)) + 4
                                   + (w.layout.num_groups if w.renderer.symm is not None and not w.renderer.fused
                                      else 0))),
     }

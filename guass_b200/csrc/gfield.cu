@@ -75,9 +75,33 @@ struct DevField {
   int32_t tile_base;  // first global tile index
   int32_t g_base;     // first global Gaussian index
   int32_t diff_base;  // first int of this field's global diff array
-  int32_t vec_ok;     // delta (and base) rows are 16-byte aligned for vector access
-  int32_t gvec_ok;    // grad rows are 16-byte aligned for vector access
+  int32_t bits;       // kFieldVecOk | kFieldGradVecOk | kFieldLists
+  int32_t slist_base; // kFieldLists: first int of this field's super-tile candidate lists
 };
+constexpr int32_t kFieldVecOk = 1;      // delta (and base) rows are 16-byte aligned for vector access
+constexpr int32_t kFieldGradVecOk = 2;  // grad rows are 16-byte aligned for vector access
+constexpr int32_t kFieldLists = 4;      // the render's candidates come from super-tile lists
+
+// Candidate lists for densified fields.  A tile's Gaussian list is rebuilt by
+// testing candidate boxes in ascending id order.  With K >= kListMinK the
+// candidates are not all K Gaussians but the list of the tile's super-tile
+// (kSuperTile x kSuperTile tiles), built once per call by the same ordered
+// scan, so every tile reads about K * (super-tile share) boxes instead of K.
+constexpr int kSuperTile = 8;
+constexpr int kListMinK = 2048;
+
+// Load balance: a 32x32 tile with more than kHeavyPairs Gaussians (clusters,
+// densified layers) is rendered by kHeavyWarps warps of 32/kHeavyWarps rows
+// each instead of the one or two warps of a regular tile, in a second launch.
+// Every element still sums its Gaussians in ascending order.
+constexpr int kHeavyPairs = 128;
+constexpr int kHeavyWarps = 4;
+constexpr int kHeavyGridCap = 2 * 148;
+// below this many warps of the regular width a 32x32 forward takes
+// kSmallGridWarps warps per tile (8 rows each): latency hiding needs warps
+constexpr int kSmallGridMinWarps = 148 * 24;
+constexpr int kSmallGridWarps = 4;
+constexpr int kHeavyChunk = 32;  // backward: pairs of a heavy tile per work item
 
 template <int NF>
 struct Params {
@@ -86,13 +110,21 @@ struct Params {
   int32_t total_tiles;
   int32_t total_g;
   int32_t tile_offset;   // render kernels: first global tile of the launch (field-range renders)
+  int32_t tile_end;      // render kernels: end of the launch's global tile range
+  int32_t pad2_;
   uint32_t* status;
   uint32_t* done;
+  uint32_t* heavy_count;  // entries in `heavy` (reset before each binning / backward)
+  int32_t* heavy;         // forward: global indices of the tiles with more than kHeavyPairs pairs;
+                          // backward: (tile, chunk) int2 work items of those tiles
+  int32_t heavy_cap;      // backward: capacity of the work-item list
+  int32_t pad3_;
   float4* records;       // [total_g][2]
   int4* boxes;           // [total_g]  (r0, r1, c0, c1)
   int64_t* goff;         // [total_g]  first partial slot of each Gaussian
   int64_t* field_pairs;  // [n]
   int32_t* diff;         // global fallback for large tile grids
+  int32_t* slist;        // super-tile candidate lists: per super-tile [count, ids...] (K + 1 ints)
   float4* partials;      // [part_cap][2]
   int64_t part_cap;      // slots in partials (backward)
   int64_t* batch_ids;    // shared-id mode or nullptr
@@ -249,6 +281,20 @@ __device__ __forceinline__ int field_of_tile(const Params<NF>& p, int t) {
   return lo;
 }
 
+// Candidates of tile (tr, tc): ascending Gaussian ids, list[i] or i itself.
+struct Cands {
+  const int32_t* list;  // nullptr: the candidates are 0 .. n-1
+  int n;
+  __device__ __forceinline__ int at(int i) const { return list ? list[i] : i; }
+};
+template <int NF>
+__device__ __forceinline__ Cands tile_candidates(const Params<NF>& p, const DevField& F, int tr, int tc) {
+  if (!(F.bits & kFieldLists)) return Cands{nullptr, F.K};
+  const int nsc = (F.ntc + kSuperTile - 1) / kSuperTile;
+  const int32_t* l = p.slist + F.slist_base + (int64_t)((tr / kSuperTile) * nsc + tc / kSuperTile) * (F.K + 1);
+  return Cands{l + 1, l[0]};
+}
+
 template <int NF>
 __device__ __forceinline__ int field_of_gaussian(const Params<NF>& p, int g) {
   int lo = 0, hi = p.n - 1;
@@ -340,7 +386,9 @@ bin_kernel(const __grid_constant__ Params<NF> p, int smem_cap_ints) {
   int64_t off = block_exclusive_scan(local, s_warp, &total);
   for (int t = t0; t < t1; ++t) {
     F.tile_ptr[t] = off;
-    off += D[(t / F.ntc) * W + (t % F.ntc)];
+    const int c = D[(t / F.ntc) * W + (t % F.ntc)];
+    off += c;
+    if (c > kHeavyPairs) p.heavy[atomicAdd(p.heavy_count, 1u)] = F.tile_base + t;
   }
   if (tid == 0) {
     F.tile_ptr[T] = total;
@@ -396,11 +444,13 @@ __global__ void __launch_bounds__(32 * kEmitWarps) emit_ids_kernel(const __grid_
     cap_left = F.ids_cap - start;
   }
   const int4* box = p.boxes + F.g_base;
+  const Cands cd = tile_candidates(p, F, tr, tc);
   int64_t found = 0;
-  for (int k0 = 0; k0 < F.K && found < count; k0 += 32) {
-    const int g = k0 + lane;
+  for (int k0 = 0; k0 < cd.n && found < count; k0 += 32) {
+    const bool cv = k0 + lane < cd.n;
+    const int g = cv ? cd.at(k0 + lane) : 0;
     bool hit = false;
-    if (g < F.K && GF_IN_BOUNDS(F.g_base + g < p.total_g)) {
+    if (cv && GF_IN_BOUNDS(g < F.K && F.g_base + g < p.total_g)) {
       const int4 b = box[g];
       hit = (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
     }
@@ -412,6 +462,41 @@ __global__ void __launch_bounds__(32 * kEmitWarps) emit_ids_kernel(const __grid_
     found += __popc(m);
   }
   if (lane == 0 && found != count) atomicOr(p.status, GF_FLAG_INTERNAL);
+}
+
+// ---------------------------------------------------------------------------
+// Super-tile candidate lists of densified fields (kFieldLists): one warp per
+// super-tile scans the field's boxes 32 at a time, in ascending id order, and
+// compacts those that reach the super-tile into [count, ids...] -- so each
+// list is ascending and so is every tile list built from it.  Grid:
+// (super-tiles / 4, fields).
+constexpr int kListWarps = 4;
+
+template <int NF>
+__global__ void __launch_bounds__(32 * kListWarps) super_list_kernel(const __grid_constant__ Params<NF> p) {
+  const DevField& F = p.f[blockIdx.y];
+  if (!(F.bits & kFieldLists)) return;
+  const int nsr = (F.ntr + kSuperTile - 1) / kSuperTile, nsc = (F.ntc + kSuperTile - 1) / kSuperTile;
+  const int s = blockIdx.x * kListWarps + (threadIdx.x >> 5);
+  if (s >= nsr * nsc) return;  // whole warps
+  const int lane = threadIdx.x & 31;
+  const int r0 = (s / nsc) * kSuperTile, c0 = (s % nsc) * kSuperTile;
+  const int r1 = r0 + kSuperTile - 1, c1 = c0 + kSuperTile - 1;
+  int32_t* list = p.slist + F.slist_base + (int64_t)s * (F.K + 1);
+  const int4* box = p.boxes + F.g_base;
+  int n = 0;
+  for (int k0 = 0; k0 < F.K; k0 += 32) {
+    const int g = k0 + lane;
+    bool hit = false;
+    if (g < F.K && GF_IN_BOUNDS(F.g_base + g < p.total_g)) {
+      const int4 b = box[g];
+      hit = (b.x <= r1) & (r0 <= b.y) & (b.z <= c1) & (c0 <= b.w);
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, hit);
+    if (hit) list[1 + n + __popc(m & ((1u << lane) - 1u))] = g;
+    n += __popc(m);
+  }
+  if (lane == 0) list[0] = n;
 }
 
 // ---------------------------------------------------------------------------
@@ -457,6 +542,7 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
   const float4* rec = p.records + 2 * (size_t)F.g_base;
   const int4* box = p.boxes + F.g_base;
   const float nclamp = p.cfg.nclamp;
+  const Cands cd = tile_candidates(p, F, tr, tc);
 
   for (int rb = 0; rb < th; rb += 32) {
     for (int cb = 0; cb < tw; cb += 32) {
@@ -471,10 +557,11 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
       }
       float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       int64_t found = 0;
-      for (int k0 = 0; k0 < F.K && found < count; k0 += kChunk) {
-        const int g = k0 + tid;
+      for (int k0 = 0; k0 < cd.n && found < count; k0 += kChunk) {
+        const bool cv = k0 + tid < cd.n;
+        const int g = cv ? cd.at(k0 + tid) : 0;
         bool hit = false;
-        if (g < F.K && GF_IN_BOUNDS(F.g_base + g < p.total_g)) {
+        if (cv && GF_IN_BOUNDS(g < F.K && F.g_base + g < p.total_g)) {
           const int4 b = box[g];
           hit = (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
         }
@@ -539,7 +626,7 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
         if (r < bh) {
           const size_t o = (size_t)r * F.in_f + q4;
           const size_t nel = (size_t)F.out_f * F.in_f;
-          if (F.vec_ok && q4 + 3 < bw && GF_IN_BOUNDS(base + o + 3 < nel)) {
+          if ((F.bits & kFieldVecOk) && q4 + 3 < bw && GF_IN_BOUNDS(base + o + 3 < nel)) {
             float4 x = make_float4(s_out[r][q4], s_out[r][q4 + 1], s_out[r][q4 + 2], s_out[r][q4 + 3]);
             if (F.base) x = add_base4(reinterpret_cast<const float*>(F.base) + base + o, x);
             store16(F.delta, F.mc, 4 * (base + o), as_u4(x));
@@ -560,7 +647,7 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
           if (r < bh) {
             const size_t o = (size_t)r * F.in_f + q8;
             const size_t nel = (size_t)F.out_f * F.in_f;
-            if (F.vec_ok && q8 + 7 < bw && GF_IN_BOUNDS(base + o + 7 < nel)) {
+            if ((F.bits & kFieldVecOk) && q8 + 7 < bw && GF_IN_BOUNDS(base + o + 7 < nel)) {
               float x[8];
 #pragma unroll
               for (int k = 0; k < 8; ++k) x[k] = s_out[r][q8 + k];
@@ -667,13 +754,10 @@ constexpr int kFwd32WarpsEx2 = GF_FWD32_WARPS_EX2;
 template <bool EX2>
 __host__ __device__ constexpr int fwd32_warps() { return EX2 ? kFwd32WarpsEx2 : kFwd32Warps; }
 
-template <int NF, bool NORM, bool CLAMP, int OUTT, bool EX2>
-__global__ void __launch_bounds__(32 * fwd32_warps<EX2>())
-render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
-  constexpr int NW = fwd32_warps<EX2>();
+template <int NF, bool NORM, bool CLAMP, int OUTT, bool EX2, int NW>
+__device__ __forceinline__ void fwd32_tile(const Params<NF>& p, int tg, bool skip_heavy,
+                                           float (*s_out)[32 / NW][36]) {
   constexpr int R = 32 / NW;  // rows per warp
-  __shared__ __align__(16) float s_out[NW][R][36];
-  const int tg = blockIdx.x + p.tile_offset;
   const int fi = field_of_tile(p, tg);
   const DevField& F = p.f[fi];
   const int t = tg - F.tile_base;
@@ -683,6 +767,7 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
   const int th = min(32, F.out_f - row0), tw = min(32, F.in_f - col0);
   const int64_t start = F.tile_ptr[t];
   const int64_t count = F.tile_ptr[t + 1] - start;
+  if (skip_heavy && count > kHeavyPairs) return;  // rendered by render_fwd32_heavy_kernel
   int64_t* ids;
   int64_t cap_left;
   if (p.batch_ids != nullptr) {
@@ -709,11 +794,13 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
 #pragma unroll
   for (int i = 0; i < R / 2; ++i) V[i] = pk2(0.0f, 0.0f);
 
+  const Cands cd = tile_candidates(p, F, tr, tc);
   int64_t found = 0;
-  for (int k0 = 0; k0 < F.K && found < count; k0 += 32) {
-    const int g = k0 + lane;
+  for (int k0 = 0; k0 < cd.n && found < count; k0 += 32) {
+    const bool cv = k0 + lane < cd.n;
+    const int g = cv ? cd.at(k0 + lane) : 0;
     bool hit = false;
-    if (g < F.K && GF_IN_BOUNDS(F.g_base + g < p.total_g)) {
+    if (cv && GF_IN_BOUNDS(g < F.K && F.g_base + g < p.total_g)) {
       const int4 b = box[g];
       hit = (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
     }
@@ -723,25 +810,34 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
       if (pos < cap_left) ids[pos] = g;
     }
     found += __popc(m);
+    // Every hit's record is fetched by the lane that tested it, all lanes at
+    // once, and handed to the warp by shuffles in ascending order: one load
+    // latency per 32 candidates instead of one per Gaussian.
+    float4 ra = make_float4(0.f, 0.f, 0.f, 0.f), rh = ra;
+    if (hit) {
+      ra = rec[2 * g];
+      rh = rec[2 * g + 1];
+    }
     if constexpr (EX2) {
       // bf16 output (GF_CFG_FWD_EXP2): the form in base 2 with the column
       // terms hoisted, q2 = dx*(g00*dx + 2*g01*dy) + g11*dy^2 (g = log2e*h),
       // and the basis 2^q2 from MUFU.EX2; the normalisation folds into the
       // amplitude.  Relative error per term ~1e-5 at worst (cancelling terms
-      // of very elongated Gaussians), far below bf16's 3.9e-3 ulp.
+      // of very elongated Gaussians), far below bf16's 3.9e-3 ulp.  The owner
+      // lane precomputes the Gaussian's constants before the hand-over.
+      const float o00 = rh.x * kLog2e, o01 = 2.0f * (rh.y * kLog2e), o11 = rh.z * kLog2e;
+      const float oamp = NORM ? ra.z * ra.w : ra.z;
+      const float nclamp2 = nclamp * kLog2e;
       while (m) {
-        const int gg = k0 + __ffs(m) - 1;
+        const int src = __ffs(m) - 1;
         m &= m - 1;
-        const float4 a = rec[2 * gg];
-        const float4 h = rec[2 * gg + 1];
-        const float dy = cc - a.y;
-        const float g00 = h.x * kLog2e, g01 = h.y * kLog2e, g11 = h.z * kLog2e;
-        const f2 G00 = pk2(g00, g00);
-        const float b1 = 2.0f * g01 * dy, c0 = g11 * dy * dy;
-        const f2 B1 = pk2(b1, b1), C0 = pk2(c0, c0), MUR = pk2(a.x, a.x);
-        const float ampn = NORM ? a.z * a.w : a.z;
+        const float mur = __shfl_sync(0xffffffffu, ra.x, src), muc = __shfl_sync(0xffffffffu, ra.y, src);
+        const float g00 = __shfl_sync(0xffffffffu, o00, src), g01x2 = __shfl_sync(0xffffffffu, o01, src);
+        const float g11 = __shfl_sync(0xffffffffu, o11, src), ampn = __shfl_sync(0xffffffffu, oamp, src);
+        const float dy = cc - muc;
+        const float b1 = g01x2 * dy, c0 = g11 * dy * dy;
+        const f2 G00 = pk2(g00, g00), B1 = pk2(b1, b1), C0 = pk2(c0, c0), MUR = pk2(mur, mur);
         const f2 AMP = pk2(ampn, ampn);
-        const float nclamp2 = nclamp * kLog2e;
 #pragma unroll
         for (int i = 0; i < R / 2; ++i) {
           const f2 DX = sub2(CR[i], MUR);
@@ -755,38 +851,44 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
         }
       }
     } else {
-    while (m) {
-      const int gg = k0 + __ffs(m) - 1;
-      m &= m - 1;
-      const float4 a = rec[2 * gg];
-      const float4 h = rec[2 * gg + 1];
-      const float dy = __fsub_rn(cc, a.y);
-      const float a01 = __fmul_rn(h.y, dy);
-      const float a11 = __fmul_rn(h.z, dy);
-      const f2 H00 = pk2(h.x, h.x), H01 = pk2(h.y, h.y), A01 = pk2(a01, a01), A11 = pk2(a11, a11);
-      const f2 DY = pk2(dy, dy), MUR = pk2(a.x, a.x), AMP = pk2(a.z, a.z);
+      while (m) {
+        const int src = __ffs(m) - 1;
+        m &= m - 1;
+        float4 a, h;
+        a.x = __shfl_sync(0xffffffffu, ra.x, src);
+        a.y = __shfl_sync(0xffffffffu, ra.y, src);
+        a.z = __shfl_sync(0xffffffffu, ra.z, src);
+        a.w = NORM ? __shfl_sync(0xffffffffu, ra.w, src) : 0.0f;
+        h.x = __shfl_sync(0xffffffffu, rh.x, src);
+        h.y = __shfl_sync(0xffffffffu, rh.y, src);
+        h.z = __shfl_sync(0xffffffffu, rh.z, src);
+        const float dy = __fsub_rn(cc, a.y);
+        const float a01 = __fmul_rn(h.y, dy);
+        const float a11 = __fmul_rn(h.z, dy);
+        const f2 H00 = pk2(h.x, h.x), H01 = pk2(h.y, h.y), A01 = pk2(a01, a01), A11 = pk2(a11, a11);
+        const f2 DY = pk2(dy, dy), MUR = pk2(a.x, a.x), AMP = pk2(a.z, a.z);
 #pragma unroll
-      for (int i = 0; i < R / 2; ++i) {
-        const f2 DX = sub2(CR[i], MUR);
-        const f2 T1 = fma2(H00, DX, A01);
-        const f2 T2 = fma2(H01, DX, A11);
-        const f2 Q = fma2(DX, T1, mul2(DY, T2));
-        float q0, q1;
-        up2(Q, q0, q1);
-        q0 = fminf(q0, 0.0f);
-        q1 = fminf(q1, 0.0f);
-        if (CLAMP) {
-          q0 = fmaxf(q0, nclamp);
-          q1 = fmaxf(q1, nclamp);
+        for (int i = 0; i < R / 2; ++i) {
+          const f2 DX = sub2(CR[i], MUR);
+          const f2 T1 = fma2(H00, DX, A01);
+          const f2 T2 = fma2(H01, DX, A11);
+          const f2 Q = fma2(DX, T1, mul2(DY, T2));
+          float q0, q1;
+          up2(Q, q0, q1);
+          q0 = fminf(q0, 0.0f);
+          q1 = fminf(q1, 0.0f);
+          if (CLAMP) {
+            q0 = fmaxf(q0, nclamp);
+            q1 = fmaxf(q1, nclamp);
+          }
+          float e0 = expf(q0), e1 = expf(q1);
+          if (NORM) {
+            e0 = __fmul_rn(e0, a.w);
+            e1 = __fmul_rn(e1, a.w);
+          }
+          V[i] = fma2(AMP, pk2(e0, e1), V[i]);
         }
-        float e0 = expf(q0), e1 = expf(q1);
-        if (NORM) {
-          e0 = __fmul_rn(e0, a.w);
-          e1 = __fmul_rn(e1, a.w);
-        }
-        V[i] = fma2(AMP, pk2(e0, e1), V[i]);
       }
-    }
     }
   }
   if (warp == 0 && lane == 0 && found != count) atomicOr(p.status, GF_FLAG_INTERNAL);
@@ -812,7 +914,7 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
       if (r < bh) {
         const size_t o = (size_t)r * F.in_f + q4;
         const size_t nel = (size_t)F.out_f * F.in_f;
-        if (F.vec_ok && q4 + 3 < tw && GF_IN_BOUNDS(base + o + 3 < nel)) {
+        if ((F.bits & kFieldVecOk) && q4 + 3 < tw && GF_IN_BOUNDS(base + o + 3 < nel)) {
           float4 x = *reinterpret_cast<const float4*>(&s_out[warp][r][q4]);
           if (F.base) x = add_base4(reinterpret_cast<const float*>(F.base) + base + o, x);
           store16(F.delta, F.mc, 4 * (base + o), as_u4(x));
@@ -835,7 +937,7 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
       if (r < bh) {
         const size_t o = (size_t)r * F.in_f + q8;
         const size_t nel = (size_t)F.out_f * F.in_f;
-        if (F.vec_ok && q8 + 7 < tw && GF_IN_BOUNDS(base + o + 7 < nel)) {
+        if ((F.bits & kFieldVecOk) && q8 + 7 < tw && GF_IN_BOUNDS(base + o + 7 < nel)) {
           float4 x0 = *reinterpret_cast<const float4*>(&s_out[warp][r][q8]);
           float4 x1 = *reinterpret_cast<const float4*>(&s_out[warp][r][q8 + 4]);
           if (F.base) {
@@ -863,6 +965,29 @@ render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
   }
   // multicast stores are published before the caller's group barrier
   if (F.mc) __threadfence_system();
+}
+
+// NW warps per tile: fwd32_warps<EX2>() normally, kSmallGridWarps when the
+// launch has too few tiles to fill the GPU with that many warps.
+template <int NF, bool NORM, bool CLAMP, int OUTT, bool EX2, int NW>
+__global__ void __launch_bounds__(32 * NW, (EX2 ? 20 : 12) * fwd32_warps<EX2>() / NW)
+render_fwd32_kernel(const __grid_constant__ Params<NF> p) {
+  __shared__ __align__(16) float s_out[NW][32 / NW][36];
+  fwd32_tile<NF, NORM, CLAMP, OUTT, EX2, NW>(p, blockIdx.x + p.tile_offset, true, s_out);
+}
+
+// The tiles the binning listed as heavy (within the launch's tile range),
+// kHeavyWarps warps each, CTAs striding over the list.
+template <int NF, bool NORM, bool CLAMP, int OUTT, bool EX2>
+__global__ void __launch_bounds__(32 * kHeavyWarps) render_fwd32_heavy_kernel(const __grid_constant__ Params<NF> p) {
+  __shared__ __align__(16) float s_out[kHeavyWarps][32 / kHeavyWarps][36];
+  const int n = (int)*reinterpret_cast<volatile uint32_t*>(p.heavy_count);
+  for (int i = blockIdx.x; i < n; i += gridDim.x) {
+    const int tg = p.heavy[i];
+    if (tg < p.tile_offset || tg >= p.tile_end) continue;
+    fwd32_tile<NF, NORM, CLAMP, OUTT, EX2, kHeavyWarps>(p, tg, false, s_out);
+    __syncwarp();
+  }
 }
 
 // Lower bound of the scaled form q' = -0.5*quad at one tile corner, minus
@@ -949,6 +1074,20 @@ bwd_prep_kernel(const __grid_constant__ Params<NF> p) {
     const int64_t T = (int64_t)F.ntr * F.ntc;
     if (total != npairs || F.tile_ptr[T] != npairs || F.tile_ptr[0] != 0)
       atomicOr(p.status, GF_FLAG_STATE);
+  }
+  // work items of the heavy tiles (32x32 tiles only: the generic backward has
+  // no heavy path)
+  if (p.cfg.tile_out == 32 && p.cfg.tile_in == 32) {
+    int2* items = reinterpret_cast<int2*>(p.heavy);
+    const int T = F.ntr * F.ntc;
+    for (int t = tid; t < T; t += bs) {
+      const int64_t c = F.tile_ptr[t + 1] - F.tile_ptr[t];
+      if (c <= kHeavyPairs || c > F.K) continue;  // (an impossible count is flagged by the render)
+      const int nch = (int)((c + kHeavyChunk - 1) / kHeavyChunk);
+      const unsigned at = atomicAdd(p.heavy_count, (unsigned)nch);
+      for (int j = 0; j < nch; ++j)
+        if (at + j < (unsigned)p.heavy_cap) items[at + j] = make_int2(F.tile_base + t, j);
+    }
   }
 }
 
@@ -1223,11 +1362,8 @@ __device__ __forceinline__ PairSums bwd32_pair_rows(const float* s_rows, const f
 }
 
 template <int NF, bool NORM, bool CLAMP, int GT, bool EX2>
-__global__ void __launch_bounds__(32 * kBwd32Warps)
-render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
-  __shared__ __align__(16) float s_rows[32];
-  __shared__ __align__(16) float s_gt[32 * kGtStride];
-  const int tg = blockIdx.x;
+__device__ __forceinline__ void bwd32_tile(const Params<NF>& p, int tg, int pair_lo, int pair_hi, bool skip_heavy,
+                                           float* s_rows, float* s_gt) {
   const int fi = field_of_tile(p, tg);
   const DevField& F = p.f[fi];
   const int t = tg - F.tile_base;
@@ -1243,13 +1379,16 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
     return;
   }
   const int count = (int)count64;
+  if (skip_heavy && count > kHeavyPairs) return;  // chunks of it go to render_bwd32_heavy_kernel
+  const int lo = pair_lo, hi = min(pair_hi, count);
+  if (lo >= hi) return;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int row0 = tr * 32, col0 = tc * 32;
   const int th = min(32, F.out_f - row0), tw = min(32, F.in_f - col0);
   if (threadIdx.x < 32) s_rows[threadIdx.x] = (threadIdx.x < th) ? F.row[row0 + threadIdx.x] : 0.0f;
   // dL/d(delta) of the tile, transposed into s_gt[col][row]
   const size_t gbase = (size_t)row0 * F.in_f + col0;
-  if (th == 32 && tw == 32 && F.gvec_ok &&
+  if (th == 32 && tw == 32 && (F.bits & kFieldGradVecOk) &&
       GF_IN_BOUNDS(gbase + (size_t)31 * F.in_f + 31 < (size_t)F.out_f * F.in_f)) {
     if (GT == GF_F32) {
 #pragma unroll
@@ -1290,7 +1429,7 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
     }
   }
   __syncthreads();
-  if (warp >= count) return;
+  if (lo + warp >= hi) return;
   const bool cval = lane < tw;
   const float cc = cval ? F.col[col0 + lane] : 0.0f;
   // Per-tile clamp test for Gaussians flagged by bwd_prep (record norm < 0):
@@ -1310,19 +1449,20 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
   const int my_ch = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
 
   // software pipeline: the next pair's id, box and record load while this one computes
-  int gid = (int)ids[warp];
-  bool okn = (ids[warp] >= 0) && (ids[warp] < F.K) && (warp == 0 || ids[warp - 1] < ids[warp]);
+  const int i0 = lo + warp;
+  int gid = (int)ids[i0];
+  bool okn = (ids[i0] >= 0) && (ids[i0] < F.K) && (i0 == 0 || ids[i0 - 1] < ids[i0]);
   int4 bn = okn ? box[gid] : make_int4(0, -1, 0, -1);
   float4 an = okn ? rec[2 * gid] : make_float4(0.f, 0.f, 0.f, 0.f);
   float4 hn = okn ? rec[2 * gid + 1] : make_float4(0.f, 0.f, 0.f, 0.f);
   int64_t gon = okn ? goff[gid] : -1;
-  for (int i = warp; i < count; i += kBwd32Warps) {
+  for (int i = i0; i < hi; i += kBwd32Warps) {
     const int4 b = bn;
     const float4 a = an, h = hn;
     const int64_t go = gon;
     const bool ok = okn && (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
     const int inext = i + kBwd32Warps;
-    if (inext < count) {
+    if (inext < hi) {
       const int64_t idn = ids[inext], idp = ids[inext - 1];
       okn = (idn >= 0) && (idn < F.K) && (idp < idn);
       gid = (int)idn;
@@ -1399,6 +1539,31 @@ render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
     } else if (lane == 0) {
       atomicOr(p.status, GF_FLAG_STATE);
     }
+  }
+}
+
+template <int NF, bool NORM, bool CLAMP, int GT, bool EX2>
+__global__ void __launch_bounds__(32 * kBwd32Warps)
+render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
+  __shared__ __align__(16) float s_rows[32];
+  __shared__ __align__(16) float s_gt[32 * kGtStride];
+  bwd32_tile<NF, NORM, CLAMP, GT, EX2>(p, blockIdx.x, 0, INT32_MAX, true, s_rows, s_gt);
+}
+
+// Chunks of kHeavyChunk pairs of the heavy tiles (listed by bwd_prep), CTAs
+// striding over the list: a tile with hundreds of pairs is spread over many
+// CTAs instead of its own four warps.
+template <int NF, bool NORM, bool CLAMP, int GT, bool EX2>
+__global__ void __launch_bounds__(32 * kBwd32Warps)
+render_bwd32_heavy_kernel(const __grid_constant__ Params<NF> p) {
+  __shared__ __align__(16) float s_rows[32];
+  __shared__ __align__(16) float s_gt[32 * kGtStride];
+  const int n = min((int)*reinterpret_cast<volatile uint32_t*>(p.heavy_count), p.heavy_cap);
+  const int2* items = reinterpret_cast<const int2*>(p.heavy);
+  for (int i = blockIdx.x; i < n; i += gridDim.x) {
+    const int2 it = items[i];
+    bwd32_tile<NF, NORM, CLAMP, GT, EX2>(p, it.x, it.y * kHeavyChunk, (it.y + 1) * kHeavyChunk, false, s_rows, s_gt);
+    __syncthreads();  // the next chunk restages the shared tile
   }
 }
 
@@ -1510,9 +1675,20 @@ gf_status fail(gf_status s, const char* fmt, ...) {
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Layout {
-  size_t hdr, records, boxes, goff, field_pairs, diff, partials, total;
+  size_t hdr, records, boxes, goff, field_pairs, diff, slist, heavy, partials, total;
   int64_t total_tiles, total_g, diff_ints, pair_cap;
+  int64_t slist_ints;  // forward: super-tile lists of the fields with K >= kListMinK (0 = none)
+  int64_t heavy_items; // backward: capacity of the heavy-tile work items
+  int max_supertiles;
 };
+
+// Ints of a field's super-tile lists, or 0 when the field scans all K boxes.
+inline int64_t field_list_ints(int64_t out_f, int64_t in_f, int64_t k, const gf_config* cfg) {
+  if (k < kListMinK) return 0;
+  const int64_t ntr = (out_f + cfg->tile_out - 1) / cfg->tile_out, ntc = (in_f + cfg->tile_in - 1) / cfg->tile_in;
+  const int64_t ns = ((ntr + kSuperTile - 1) / kSuperTile) * ((ntc + kSuperTile - 1) / kSuperTile);
+  return ns * (k + 1);
+}
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
@@ -1581,6 +1757,18 @@ Layout layout(const gf_config* cfg, const gf_batch* batch, gf_pass pass) {
     const int64_t nd = (ntr + 1) * (ntc + 1);
     if (nd > kBinSmemCapInts) L.diff_ints += nd;
     if (!batch->ids) L.pair_cap += f.ids_capacity;
+    if (pass == GF_PASS_FORWARD) {
+      const int64_t li = field_list_ints(f.out_features, f.in_features, f.num_gaussians, cfg);
+      if (li > 0) {
+        L.slist_ints += li;
+        const int64_t ns = li / (f.num_gaussians + 1);
+        if (ns > L.max_supertiles) L.max_supertiles = (int)ns;
+      }
+    }
+  }
+  if (L.slist_ints > INT32_MAX) {  // beyond 32-bit list offsets: every field scans all its boxes
+    L.slist_ints = 0;
+    L.max_supertiles = 0;
   }
   if (batch->ids) L.pair_cap = batch->ids_capacity;
   size_t off = 0;
@@ -1590,6 +1778,15 @@ Layout layout(const gf_config* cfg, const gf_batch* batch, gf_pass pass) {
   L.goff = off; off = align256(off + 8 * (size_t)L.total_g);
   L.field_pairs = off; off = align256(off + 8 * (size_t)batch->num_fields);
   L.diff = off; off = align256(off + 4 * (size_t)L.diff_ints);
+  L.slist = off; off = align256(off + 4 * (size_t)L.slist_ints);
+  L.heavy = off;
+  if (pass == GF_PASS_FORWARD) {
+    off = align256(off + 4 * (size_t)L.total_tiles);
+  } else {  // (tile, chunk) items: at most pairs / kHeavyChunk + one partial chunk per tile
+    L.heavy_items = L.pair_cap / kHeavyChunk + L.total_tiles;
+    if (L.heavy_items > INT32_MAX) L.heavy_items = INT32_MAX;
+    off = align256(off + 8 * (size_t)L.heavy_items);
+  }
   L.partials = off;
   if (pass == GF_PASS_BACKWARD) off = align256(off + 32 * (size_t)L.pair_cap);
   L.total = off;
@@ -1612,17 +1809,23 @@ void fill_params(Params<NF>& P, const gf_config* cfg, const gf_batch* batch, con
   P.total_g = (int32_t)L.total_g;
   P.status = reinterpret_cast<uint32_t*>(ws + L.hdr);
   P.done = reinterpret_cast<uint32_t*>(ws + L.hdr + 4);
+  P.heavy_count = reinterpret_cast<uint32_t*>(ws + L.hdr + 8);
+  P.heavy = reinterpret_cast<int32_t*>(ws + L.heavy);
+  P.tile_end = (int32_t)L.total_tiles;
+  P.heavy_cap = (int32_t)L.heavy_items;
   P.records = reinterpret_cast<float4*>(ws + L.records);
   P.boxes = reinterpret_cast<int4*>(ws + L.boxes);
   P.goff = reinterpret_cast<int64_t*>(ws + L.goff);
   P.field_pairs = reinterpret_cast<int64_t*>(ws + L.field_pairs);
   P.diff = reinterpret_cast<int32_t*>(ws + L.diff);
+  P.slist = reinterpret_cast<int32_t*>(ws + L.slist);
   P.partials = reinterpret_cast<float4*>(ws + L.partials);
   P.part_cap = L.pair_cap;
   P.batch_ids = batch->ids;
   P.batch_cap = batch->ids_capacity;
   P.pair_base = batch->pair_base;
   int32_t tile_base = 0, g_base = 0, diff_base = 0;
+  int64_t slist_base = 0;
   int64_t part_base = 0;
   const size_t esz = cfg->out_dtype == GF_BF16 ? 2 : 4;
   for (int i = 0; i < batch->num_fields; ++i) {
@@ -1649,12 +1852,24 @@ void fill_params(Params<NF>& P, const gf_config* cfg, const gf_batch* batch, con
     tile_base += d.ntr * d.ntc;
     g_base += d.K;
     const size_t vec = 16 / esz;
-    d.vec_ok = ((reinterpret_cast<uintptr_t>(s.delta) & 15u) == 0) &&
-               ((reinterpret_cast<uintptr_t>(s.base_weight) & 15u) == 0) && (s.in_features % (int64_t)vec == 0) &&
-               (cfg->tile_in % (int64_t)vec == 0);
+    d.bits = 0;
+    if (((reinterpret_cast<uintptr_t>(s.delta) & 15u) == 0) &&
+        ((reinterpret_cast<uintptr_t>(s.base_weight) & 15u) == 0) && (s.in_features % (int64_t)vec == 0) &&
+        (cfg->tile_in % (int64_t)vec == 0))
+      d.bits |= kFieldVecOk;
+    d.slist_base = 0;
+    if (L.slist_ints > 0) {
+      const int64_t li = field_list_ints(s.out_features, s.in_features, s.num_gaussians, cfg);
+      if (li > 0) {
+        d.bits |= kFieldLists;
+        d.slist_base = (int32_t)slist_base;
+        slist_base += li;
+      }
+    }
     const int64_t gvec = cfg->grad_dtype == GF_BF16 ? 8 : 4;
-    d.gvec_ok = ((reinterpret_cast<uintptr_t>(s.grad_delta) & 15u) == 0) && (s.in_features % gvec == 0) &&
-                (cfg->tile_in % gvec == 0);
+    if (((reinterpret_cast<uintptr_t>(s.grad_delta) & 15u) == 0) && (s.in_features % gvec == 0) &&
+        (cfg->tile_in % gvec == 0))
+      d.bits |= kFieldGradVecOk;
   }
 }
 
@@ -1703,8 +1918,15 @@ gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout&
   if (stages & GF_STAGE_BIN) {
     NvtxRange r("gfield.bin");
     trace_mark(st);
+    if (cudaMemsetAsync(p.heavy_count, 0, sizeof(uint32_t), st) != cudaSuccess)
+      return fail(GF_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(cudaGetLastError()));
     bin_kernel<NF><<<p.n, kBinThreads, smem, st>>>(p, kBinSmemCapInts);
     GF_LAUNCH_CHECK("bin_kernel");
+    if (L.slist_ints > 0) {
+      super_list_kernel<NF><<<dim3((unsigned)ceil_div(L.max_supertiles, kListWarps), (unsigned)p.n), 32 * kListWarps, 0,
+                              st>>>(p);
+      GF_LAUNCH_CHECK("super_list_kernel");
+    }
     if (!(stages & GF_STAGE_RENDER)) {
       // the BIN stage alone also writes the id lists (the render normally does)
       emit_ids_kernel<NF><<<(int)ceil_div(L.total_tiles, kEmitWarps), 32 * kEmitWarps, 0, st>>>(p);
@@ -1721,17 +1943,29 @@ gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout&
     const int t0 = p.f[first_field].tile_base;
     const int t1 = first_field + num_fields < p.n ? p.f[first_field + num_fields].tile_base : (int)L.total_tiles;
     p.tile_offset = t0;
+    p.tile_end = t1;
     grid = t1 - t0;
     if (grid <= 0) return GF_OK;
   }
 #define GF_FWD(N, C, O)                                                                         \
   do {                                                                                          \
-    if (fast32 && O == GF_BF16 && (p.cfg.flags & GF_CFG_FWD_EXP2))                               \
-      render_fwd32_kernel<NF, N, C, O, (O == GF_BF16)><<<grid, 32 * fwd32_warps<(O == GF_BF16)>(), 0, st>>>(p); \
-    else if (fast32) render_fwd32_kernel<NF, N, C, O, false><<<grid, 32 * kFwd32Warps, 0, st>>>(p); \
-    else render_fwd_kernel<NF, N, C, O><<<grid, kRenderThreads, 0, st>>>(p);                    \
+    if (fast32 && O == GF_BF16 && (p.cfg.flags & GF_CFG_FWD_EXP2)) {                             \
+      constexpr bool X = (O == GF_BF16);                                                        \
+      if (grid * fwd32_warps<X>() < kSmallGridMinWarps)                                         \
+        render_fwd32_kernel<NF, N, C, O, X, kSmallGridWarps><<<grid, 32 * kSmallGridWarps, 0, st>>>(p); \
+      else                                                                                      \
+        render_fwd32_kernel<NF, N, C, O, X, fwd32_warps<X>()><<<grid, 32 * fwd32_warps<X>(), 0, st>>>(p); \
+      render_fwd32_heavy_kernel<NF, N, C, O, X><<<heavy_grid, 32 * kHeavyWarps, 0, st>>>(p);   \
+    } else if (fast32) {                                                                        \
+      if (grid * kFwd32Warps < kSmallGridMinWarps)                                              \
+        render_fwd32_kernel<NF, N, C, O, false, kSmallGridWarps><<<grid, 32 * kSmallGridWarps, 0, st>>>(p); \
+      else                                                                                      \
+        render_fwd32_kernel<NF, N, C, O, false, kFwd32Warps><<<grid, 32 * kFwd32Warps, 0, st>>>(p); \
+      render_fwd32_heavy_kernel<NF, N, C, O, false><<<heavy_grid, 32 * kHeavyWarps, 0, st>>>(p); \
+    } else render_fwd_kernel<NF, N, C, O><<<grid, kRenderThreads, 0, st>>>(p);                  \
   } while (0)
   const bool fast32 = cfg->tile_out == 32 && cfg->tile_in == 32;
+  const int heavy_grid = grid < kHeavyGridCap ? grid : kHeavyGridCap;  // CTAs striding over the heavy tiles
   if (cfg->out_dtype == GF_F32) {
     if (norm) { if (clamp) GF_FWD(true, true, GF_F32); else GF_FWD(true, false, GF_F32); }
     else { if (clamp) GF_FWD(false, true, GF_F32); else GF_FWD(false, false, GF_F32); }
@@ -1748,8 +1982,14 @@ gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout&
 template <int NF, bool N, bool C, int G>
 cudaError_t launch_bwd_render(const Params<NF>& p, int grid, size_t smem, cudaStream_t st) {
   if (p.cfg.tile_out == 32 && p.cfg.tile_in == 32) {
-    if (p.cfg.flags & GF_CFG_BWD_EXP2) render_bwd32_kernel<NF, N, C, G, true><<<grid, 32 * kBwd32Warps, 0, st>>>(p);
-    else render_bwd32_kernel<NF, N, C, G, false><<<grid, 32 * kBwd32Warps, 0, st>>>(p);
+    const int hgrid = grid < kHeavyGridCap ? grid : kHeavyGridCap;
+    if (p.cfg.flags & GF_CFG_BWD_EXP2) {
+      render_bwd32_kernel<NF, N, C, G, true><<<grid, 32 * kBwd32Warps, 0, st>>>(p);
+      render_bwd32_heavy_kernel<NF, N, C, G, true><<<hgrid, 32 * kBwd32Warps, 0, st>>>(p);
+    } else {
+      render_bwd32_kernel<NF, N, C, G, false><<<grid, 32 * kBwd32Warps, 0, st>>>(p);
+      render_bwd32_heavy_kernel<NF, N, C, G, false><<<hgrid, 32 * kBwd32Warps, 0, st>>>(p);
+    }
     return cudaSuccess;
   }
   const cudaError_t e = allow_dynamic_smem<render_bwd_kernel<NF, N, C, G>>(kBwdSmemCapFloats * 4);
@@ -1767,6 +2007,8 @@ gf_status run_backward(const gf_config* cfg, const gf_batch* batch, const Layout
   {
     NvtxRange r("gfield.bwd_prep");
     trace_mark(st);
+    if (cudaMemsetAsync(p.heavy_count, 0, sizeof(uint32_t), st) != cudaSuccess)
+      return fail(GF_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(cudaGetLastError()));
     bwd_prep_kernel<NF><<<p.n, kBinThreads, 0, st>>>(p);
     GF_LAUNCH_CHECK("bwd_prep_kernel");
     trace_mark(st);
@@ -2034,16 +2276,32 @@ gf_status noalloc_launch(Params<NF>& p, const gf_config* cfg, const gf_batch* ba
   if (e != cudaSuccess) return fail(GF_ERR_CUDA, "gf_forward_noalloc: %s", cudaGetErrorString(e));
   bin_kernel<NF><<<p.n, kBinThreads, sizeof(int) * (size_t)max_nd, st>>>(p, kBinSmemCapInts);
   GF_LAUNCH_CHECK("bin_kernel");
+  if (L.slist_ints > 0) {
+    super_list_kernel<NF><<<dim3((unsigned)ceil_div(L.max_supertiles, kListWarps), (unsigned)p.n), 32 * kListWarps, 0,
+                            st>>>(p);
+    GF_LAUNCH_CHECK("super_list_kernel");
+  }
   const bool norm = p.cfg.normalize, clamp = p.cfg.has_clamp;
   const int grid = (int)L.total_tiles;
 #define GF_FWD(N, C, O)                                                                         \
   do {                                                                                          \
-    if (fast32 && O == GF_BF16 && (p.cfg.flags & GF_CFG_FWD_EXP2))                               \
-      render_fwd32_kernel<NF, N, C, O, (O == GF_BF16)><<<grid, 32 * fwd32_warps<(O == GF_BF16)>(), 0, st>>>(p); \
-    else if (fast32) render_fwd32_kernel<NF, N, C, O, false><<<grid, 32 * kFwd32Warps, 0, st>>>(p); \
-    else render_fwd_kernel<NF, N, C, O><<<grid, kRenderThreads, 0, st>>>(p);                    \
+    if (fast32 && O == GF_BF16 && (p.cfg.flags & GF_CFG_FWD_EXP2)) {                             \
+      constexpr bool X = (O == GF_BF16);                                                        \
+      if (grid * fwd32_warps<X>() < kSmallGridMinWarps)                                         \
+        render_fwd32_kernel<NF, N, C, O, X, kSmallGridWarps><<<grid, 32 * kSmallGridWarps, 0, st>>>(p); \
+      else                                                                                      \
+        render_fwd32_kernel<NF, N, C, O, X, fwd32_warps<X>()><<<grid, 32 * fwd32_warps<X>(), 0, st>>>(p); \
+      render_fwd32_heavy_kernel<NF, N, C, O, X><<<heavy_grid, 32 * kHeavyWarps, 0, st>>>(p);   \
+    } else if (fast32) {                                                                        \
+      if (grid * kFwd32Warps < kSmallGridMinWarps)                                              \
+        render_fwd32_kernel<NF, N, C, O, false, kSmallGridWarps><<<grid, 32 * kSmallGridWarps, 0, st>>>(p); \
+      else                                                                                      \
+        render_fwd32_kernel<NF, N, C, O, false, kFwd32Warps><<<grid, 32 * kFwd32Warps, 0, st>>>(p); \
+      render_fwd32_heavy_kernel<NF, N, C, O, false><<<heavy_grid, 32 * kHeavyWarps, 0, st>>>(p); \
+    } else render_fwd_kernel<NF, N, C, O><<<grid, kRenderThreads, 0, st>>>(p);                  \
   } while (0)
   const bool fast32 = cfg->tile_out == 32 && cfg->tile_in == 32;
+  const int heavy_grid = grid < kHeavyGridCap ? grid : kHeavyGridCap;  // CTAs striding over the heavy tiles
   if (cfg->out_dtype == GF_F32) {
     if (norm) { if (clamp) GF_FWD(true, true, GF_F32); else GF_FWD(true, false, GF_F32); }
     else { if (clamp) GF_FWD(false, true, GF_F32); else GF_FWD(false, false, GF_F32); }

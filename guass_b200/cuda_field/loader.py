@@ -26,8 +26,14 @@ def build_instructions() -> str:
             f"(nvcc, sm_100a). Sources: {', '.join(get_source_paths())}; library: {_lib.LIB_PATH}")
 
 
-@lru_cache(maxsize=1)
 def load_extension(*, verbose: bool = False):
+    """The one extension object of this process (``verbose`` is accepted for
+    the reference's signature; nothing is built here)."""
+    return _extension()
+
+
+@lru_cache(maxsize=1)
+def _extension():
     from guass_b200.cuda_field._ext import GaussianFieldExtension
 
     return GaussianFieldExtension()

@@ -161,4 +161,25 @@ def cfg3(seed: int = 0, k: int = 256) -> list[FieldInputs]:
     return fields
 
 
+def densified(k: int, seed: int = 0) -> FieldInputs:
+    """A 1280x1280 field after densification (gaussian_peft/trainers/
+    base_trainer.py:127-220 clones and splits Gaussians, so K grows while each
+    one shrinks): K Gaussians with log s ~ N(log(0.02 * sqrt(1024 / K)), 0.3)
+    (the covered area stays about that of cfg2's K=1024), 25% elongated, half
+    the means in 8 blobs as cfg2."""
+    return make_field(1280, 1280, k, seed=seed, log_scale_mean=math.log(0.02 * math.sqrt(1024.0 / k)),
+                      log_scale_std=0.3, elongated_frac=0.25, blob_frac=0.5, name=f"dense{k}")
+
+
+def degenerate_scan(k: int, out_f: int = 1280, in_f: int = 1280) -> FieldInputs:
+    """K tiny Gaussians all inside the first tile of a field: every other tile
+    has no pair, so a render of it costs the per-tile candidate scan over the
+    K boxes (plus one tile's K x 1024 evaluations) -- an upper bound on the
+    scan's share of a real render with the same K."""
+    f = make_field(out_f, in_f, k, seed=7, log_scale_mean=math.log(1e-4), log_scale_std=0.1)
+    f.mu[:, 0] = -1.0 + 1.0 / out_f
+    f.mu[:, 1] = -1.0 + 1.0 / in_f
+    return f
+
+
 CONFIGS = {"cfg0": cfg0, "cfg1": cfg1, "cfg2": cfg2}
