@@ -37,12 +37,9 @@ constexpr double kTwoPi = 6.28318530717958647692;
 
 constexpr int kBinThreads = 512;
 constexpr int kRenderThreads = 256;  // 8 warps; fast path tile = 32x32
-constexpr int kChunk = 256;          // candidate Gaussians tested per pass
+constexpr int kChunk = 256;          // tile-list entries (or candidates) taken per pass
 constexpr int kBinSmemCapInts = 24 * 1024;          // 96 KB diff array in smem
 constexpr int kBwdSmemCapFloats = 24 * 1024;        // 96 KB grad tile in smem
-// Cfg.flags bit set by the host for a RENDER-only stage: the BIN stage has
-// already written the per-tile id lists (emit_ids_kernel), the render does not.
-constexpr uint32_t kFlagIdsWritten = 0x80000000u;
 
 struct Cfg {
   int32_t tile_out, tile_in;
@@ -75,20 +72,11 @@ struct DevField {
   int32_t tile_base;  // first global tile index
   int32_t g_base;     // first global Gaussian index
   int32_t diff_base;  // first int of this field's global diff array
-  int32_t bits;       // kFieldVecOk | kFieldGradVecOk | kFieldLists
-  int32_t slist_base; // kFieldLists: first int of this field's super-tile candidate lists
+  int32_t bits;       // kFieldVecOk | kFieldGradVecOk
+  int32_t pad_;
 };
 constexpr int32_t kFieldVecOk = 1;      // delta (and base) rows are 16-byte aligned for vector access
 constexpr int32_t kFieldGradVecOk = 2;  // grad rows are 16-byte aligned for vector access
-constexpr int32_t kFieldLists = 4;      // the render's candidates come from super-tile lists
-
-// Candidate lists for densified fields.  A tile's Gaussian list is rebuilt by
-// testing candidate boxes in ascending id order.  With K >= kListMinK the
-// candidates are not all K Gaussians but the list of the tile's super-tile
-// (kSuperTile x kSuperTile tiles), built once per call by the same ordered
-// scan, so every tile reads about K * (super-tile share) boxes instead of K.
-constexpr int kSuperTile = 8;
-constexpr int kListMinK = 2048;
 
 // Load balance: a 32x32 tile with more than kHeavyPairs Gaussians (clusters,
 // densified layers) is rendered by kHeavyWarps warps of 32/kHeavyWarps rows
@@ -124,7 +112,7 @@ struct Params {
   int64_t* goff;         // [total_g]  first partial slot of each Gaussian
   int64_t* field_pairs;  // [n]
   int32_t* diff;         // global fallback for large tile grids
-  int32_t* slist;        // super-tile candidate lists: per super-tile [count, ids...] (K + 1 ints)
+  int32_t* cursor;       // forward: per tile, the next free slot of its id list (pair emission)
   float4* partials;      // [part_cap][2]
   int64_t part_cap;      // slots in partials (backward)
   int64_t* batch_ids;    // shared-id mode or nullptr
@@ -281,20 +269,6 @@ __device__ __forceinline__ int field_of_tile(const Params<NF>& p, int t) {
   return lo;
 }
 
-// Candidates of tile (tr, tc): ascending Gaussian ids, list[i] or i itself.
-struct Cands {
-  const int32_t* list;  // nullptr: the candidates are 0 .. n-1
-  int n;
-  __device__ __forceinline__ int at(int i) const { return list ? list[i] : i; }
-};
-template <int NF>
-__device__ __forceinline__ Cands tile_candidates(const Params<NF>& p, const DevField& F, int tr, int tc) {
-  if (!(F.bits & kFieldLists)) return Cands{nullptr, F.K};
-  const int nsc = (F.ntc + kSuperTile - 1) / kSuperTile;
-  const int32_t* l = p.slist + F.slist_base + (int64_t)((tr / kSuperTile) * nsc + tc / kSuperTile) * (F.K + 1);
-  return Cands{l + 1, l[0]};
-}
-
 template <int NF>
 __device__ __forceinline__ int field_of_gaussian(const Params<NF>& p, int g) {
   int lo = 0, hi = p.n - 1;
@@ -388,6 +362,7 @@ bin_kernel(const __grid_constant__ Params<NF> p, int smem_cap_ints) {
     F.tile_ptr[t] = off;
     const int c = D[(t / F.ntc) * W + (t % F.ntc)];
     off += c;
+    p.cursor[F.tile_base + t] = 0;
     if (c > kHeavyPairs) p.heavy[atomicAdd(p.heavy_count, 1u)] = F.tile_base + t;
   }
   if (tid == 0) {
@@ -414,89 +389,177 @@ bin_kernel(const __grid_constant__ Params<NF> p, int smem_cap_ints) {
   }
 }
 
-// ---------------------------------------------------------------------------
-// BIN stage on its own (gf_forward_stages): the per-tile id lists, so that work
-// which reads them -- the backward -- can start before the render.  One warp
-// per tile tests the field's boxes 32 at a time by ballot, in ascending id
-// order: the same order and positions at which the render kernels write the
-// lists when they run the whole forward.
-constexpr int kEmitWarps = 4;
-
+// Tile list of (tile t, its ids slot): where the BIN stage writes the tile's
+// Gaussian ids and how many fit (less than the count when the caller's id
+// buffer is too small; the capacity flag is raised by bin_kernel then).
 template <int NF>
-__global__ void __launch_bounds__(32 * kEmitWarps) emit_ids_kernel(const __grid_constant__ Params<NF> p) {
-  const int tg = blockIdx.x * kEmitWarps + (threadIdx.x >> 5);
-  if (tg >= p.total_tiles) return;  // whole warps
-  const int lane = threadIdx.x & 31;
-  const int fi = field_of_tile(p, tg);
-  const DevField& F = p.f[fi];
-  const int t = tg - F.tile_base;
-  const int tr = t / F.ntc, tc = t % F.ntc;
-  const int64_t start = F.tile_ptr[t];
-  const int64_t count = F.tile_ptr[t + 1] - start;
+struct TileIds {
   int64_t* ids;
-  int64_t cap_left;
+  int64_t count, cap_left;
+  __device__ __forceinline__ bool complete() const { return count <= cap_left; }
+};
+template <int NF>
+__device__ __forceinline__ TileIds<NF> tile_ids(const Params<NF>& p, int fi, int t) {
+  const DevField& F = p.f[fi];
+  const int64_t start = F.tile_ptr[t];
+  TileIds<NF> r;
+  r.count = F.tile_ptr[t + 1] - start;
   if (p.batch_ids != nullptr) {
     const int64_t b = p.pair_base[fi];
-    ids = p.batch_ids + b + start;
-    cap_left = p.batch_cap - b - start;
+    r.ids = p.batch_ids + b + start;
+    r.cap_left = p.batch_cap - b - start;
   } else {
-    ids = F.ids + start;
-    cap_left = F.ids_cap - start;
+    r.ids = F.ids + start;
+    r.cap_left = F.ids_cap - start;
   }
+  return r;
+}
+
+// ---------------------------------------------------------------------------
+// Forward kernel 1b: pair emission.  One warp per Gaussian walks the tiles of
+// its box; each (tile, Gaussian) pair takes the next slot of the tile's list
+// from a per-tile cursor (zeroed by bin_kernel).  Slots within a tile come out
+// in arbitrary order; sort_tiles_kernel / sort_heavy_kernel restore ascending
+// id order, which is the reference's stable (tile, id) sort order
+// (forward.cu:211-241, 469).  O(pairs), no per-tile candidate scan.
+constexpr int kEmitWarps = 8;
+
+template <int NF>
+__global__ void __launch_bounds__(32 * kEmitWarps) emit_pairs_kernel(const __grid_constant__ Params<NF> p) {
+  const int G = blockIdx.x * kEmitWarps + (threadIdx.x >> 5);
+  if (G >= p.total_g) return;  // whole warps
+  const int lane = threadIdx.x & 31;
+  const int fi = field_of_gaussian(p, G);
+  const DevField& F = p.f[fi];
+  const int g = G - F.g_base;
+  const int4 b = p.boxes[G];
+  const int bw = b.w - b.z + 1;
+  const int nb = (b.y - b.x + 1) * bw;
+  int64_t* base;
+  int64_t cap;
+  if (p.batch_ids != nullptr) {
+    const int64_t pb = p.pair_base[fi];
+    base = p.batch_ids + pb;
+    cap = p.batch_cap - pb;
+  } else {
+    base = F.ids;
+    cap = F.ids_cap;
+  }
+  for (int j = lane; j < nb; j += 32) {
+    const int t = (b.x + j / bw) * F.ntc + b.z + j % bw;
+    const int64_t at = F.tile_ptr[t] + atomicAdd(&p.cursor[F.tile_base + t], 1);
+    if (at < cap) base[at] = g;
+  }
+}
+
+struct WarpSync {
+  __device__ __forceinline__ void operator()() const { __syncwarp(); }
+};
+struct BlockSync {
+  __device__ __forceinline__ void operator()() const { __syncthreads(); }
+};
+
+// Bitonic sort of s[0, n) ascending (n a power of two), by `nt` cooperating
+// threads of index `i0`; `sync` orders the stages.
+template <typename Sync>
+__device__ __forceinline__ void bitonic_sort(int32_t* s, int n, int i0, int nt, Sync sync) {
+  for (int k = 2; k <= n; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = i0; i < n; i += nt) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const int32_t a = s[i], c = s[ixj];
+          if ((a > c) == ((i & k) == 0)) {
+            s[i] = c;
+            s[ixj] = a;
+          }
+        }
+      }
+      sync();
+    }
+  }
+}
+
+// The ordered scan of a tile's candidates (every box of the field, 32 at a
+// time, in ascending id order) -- the fallback for a tile list too long to
+// sort in shared memory.  One warp; writes the list.
+template <int NF>
+__device__ __forceinline__ void scan_tile_list(const Params<NF>& p, const DevField& F, int tr, int tc, const TileIds<NF>& L) {
+  const int lane = threadIdx.x & 31;
   const int4* box = p.boxes + F.g_base;
-  const Cands cd = tile_candidates(p, F, tr, tc);
   int64_t found = 0;
-  for (int k0 = 0; k0 < cd.n && found < count; k0 += 32) {
-    const bool cv = k0 + lane < cd.n;
-    const int g = cv ? cd.at(k0 + lane) : 0;
+  for (int k0 = 0; k0 < F.K && found < L.count; k0 += 32) {
+    const int g = k0 + lane;
     bool hit = false;
-    if (cv && GF_IN_BOUNDS(g < F.K && F.g_base + g < p.total_g)) {
+    if (g < F.K && GF_IN_BOUNDS(F.g_base + g < p.total_g)) {
       const int4 b = box[g];
       hit = (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
     }
     const unsigned m = __ballot_sync(0xffffffffu, hit);
     if (hit) {
       const int64_t pos = found + __popc(m & ((1u << lane) - 1u));
-      if (pos < cap_left) ids[pos] = g;
+      if (pos < L.cap_left) L.ids[pos] = g;
     }
     found += __popc(m);
   }
-  if (lane == 0 && found != count) atomicOr(p.status, GF_FLAG_INTERNAL);
+  if (lane == 0 && found != L.count) atomicOr(p.status, GF_FLAG_INTERNAL);
 }
 
-// ---------------------------------------------------------------------------
-// Super-tile candidate lists of densified fields (kFieldLists): one warp per
-// super-tile scans the field's boxes 32 at a time, in ascending id order, and
-// compacts those that reach the super-tile into [count, ids...] -- so each
-// list is ascending and so is every tile list built from it.  Grid:
-// (super-tiles / 4, fields).
-constexpr int kListWarps = 4;
+// Forward kernel 1c: sort every tile list of at most kHeavyPairs ids, one
+// warp per tile, in shared memory (ids are < 2^31).  Longer lists are in the
+// heavy list and sorted by sort_heavy_kernel.
+constexpr int kSortWarps = 4;
 
 template <int NF>
-__global__ void __launch_bounds__(32 * kListWarps) super_list_kernel(const __grid_constant__ Params<NF> p) {
-  const DevField& F = p.f[blockIdx.y];
-  if (!(F.bits & kFieldLists)) return;
-  const int nsr = (F.ntr + kSuperTile - 1) / kSuperTile, nsc = (F.ntc + kSuperTile - 1) / kSuperTile;
-  const int s = blockIdx.x * kListWarps + (threadIdx.x >> 5);
-  if (s >= nsr * nsc) return;  // whole warps
-  const int lane = threadIdx.x & 31;
-  const int r0 = (s / nsc) * kSuperTile, c0 = (s % nsc) * kSuperTile;
-  const int r1 = r0 + kSuperTile - 1, c1 = c0 + kSuperTile - 1;
-  int32_t* list = p.slist + F.slist_base + (int64_t)s * (F.K + 1);
-  const int4* box = p.boxes + F.g_base;
-  int n = 0;
-  for (int k0 = 0; k0 < F.K; k0 += 32) {
-    const int g = k0 + lane;
-    bool hit = false;
-    if (g < F.K && GF_IN_BOUNDS(F.g_base + g < p.total_g)) {
-      const int4 b = box[g];
-      hit = (b.x <= r1) & (r0 <= b.y) & (b.z <= c1) & (c0 <= b.w);
+__global__ void __launch_bounds__(32 * kSortWarps) sort_tiles_kernel(const __grid_constant__ Params<NF> p) {
+  __shared__ int32_t s_keys[kSortWarps][kHeavyPairs];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tg = blockIdx.x * kSortWarps + warp;
+  if (tg >= p.total_tiles) return;  // whole warps
+  const int fi = field_of_tile(p, tg);
+  const TileIds<NF> L = tile_ids(p, fi, tg - p.f[fi].tile_base);
+  const int n0 = (int)L.count;
+  if (n0 <= 1 || n0 > kHeavyPairs || !L.complete()) return;
+  int n = 32;
+  while (n < n0) n <<= 1;
+  int32_t* s = s_keys[warp];
+  for (int i = lane; i < n; i += 32) s[i] = i < n0 ? (int32_t)L.ids[i] : INT32_MAX;
+  __syncwarp();
+  bitonic_sort(s, n, lane, 32, WarpSync{});
+  for (int i = lane; i < n0; i += 32) L.ids[i] = s[i];
+}
+
+// The heavy tiles' lists (more than kHeavyPairs ids): one CTA per tile,
+// striding over the heavy list; lists beyond kSortCap ids are rebuilt by the
+// ordered scan instead.
+constexpr int kSortCap = 8192;
+constexpr int kSortThreads = 512;
+
+template <int NF>
+__global__ void __launch_bounds__(kSortThreads) sort_heavy_kernel(const __grid_constant__ Params<NF> p) {
+  __shared__ int32_t s[kSortCap];
+  const int nh = (int)*reinterpret_cast<volatile uint32_t*>(p.heavy_count);
+  for (int h = blockIdx.x; h < nh; h += gridDim.x) {
+    const int tg = p.heavy[h];
+    const int fi = field_of_tile(p, tg);
+    const DevField& F = p.f[fi];
+    const int t = tg - F.tile_base;
+    const TileIds<NF> L = tile_ids(p, fi, t);
+    const int64_t n0 = L.count;
+    if (!L.complete()) continue;
+    if (n0 > kSortCap) {
+      if (threadIdx.x < 32) scan_tile_list(p, F, t / F.ntc, t % F.ntc, L);
+      __syncthreads();
+      continue;
     }
-    const unsigned m = __ballot_sync(0xffffffffu, hit);
-    if (hit) list[1 + n + __popc(m & ((1u << lane) - 1u))] = g;
-    n += __popc(m);
+    int n = 32;
+    while (n < n0) n <<= 1;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s[i] = i < n0 ? (int32_t)L.ids[i] : INT32_MAX;
+    __syncthreads();
+    bitonic_sort(s, n, (int)threadIdx.x, (int)blockDim.x, BlockSync{});
+    for (int i = threadIdx.x; i < n0; i += blockDim.x) L.ids[i] = s[i];
+    __syncthreads();
   }
-  if (lane == 0) list[0] = n;
 }
 
 // ---------------------------------------------------------------------------
@@ -542,11 +605,13 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
   const float4* rec = p.records + 2 * (size_t)F.g_base;
   const int4* box = p.boxes + F.g_base;
   const float nclamp = p.cfg.nclamp;
-  const Cands cd = tile_candidates(p, F, tr, tc);
+  // the tile's sorted list from the BIN stage; if the id buffer could not
+  // hold it, the ordered scan of every box of the field (same order)
+  const bool listed = count <= cap_left;
+  const int ncand = listed ? (int)count : F.K;
 
   for (int rb = 0; rb < th; rb += 32) {
     for (int cb = 0; cb < tw; cb += 32) {
-      const bool first = (rb == 0 && cb == 0);
       const int c = cb + lane;
       const float cc = (c < tw) ? F.col[col0 + c] : 0.0f;
       float cr[4];
@@ -557,13 +622,19 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
       }
       float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       int64_t found = 0;
-      for (int k0 = 0; k0 < cd.n && found < count; k0 += kChunk) {
-        const bool cv = k0 + tid < cd.n;
-        const int g = cv ? cd.at(k0 + tid) : 0;
+      for (int k0 = 0; k0 < ncand && found < count; k0 += kChunk) {
+        int g = 0;
         bool hit = false;
-        if (cv && GF_IN_BOUNDS(g < F.K && F.g_base + g < p.total_g)) {
-          const int4 b = box[g];
-          hit = (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
+        if (k0 + tid < ncand) {
+          if (listed) {
+            const int64_t v = ids[k0 + tid];
+            g = (int)v;
+            hit = v >= 0 && v < F.K;
+          } else if (GF_IN_BOUNDS(F.g_base + k0 + tid < p.total_g)) {
+            g = k0 + tid;
+            const int4 b = box[g];
+            hit = (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
+          }
         }
         const unsigned m = __ballot_sync(0xffffffffu, hit);
         if (lane == 0) s_wcnt[warp] = __popc(m);
@@ -578,7 +649,6 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
         if (hit) {
           const int pos = before + __popc(m & ((1u << lane) - 1u));
           s_list[pos] = g;
-          if (first && found + pos < cap_left && !(p.cfg.flags & kFlagIdsWritten)) ids[found + pos] = g;
         }
         __syncthreads();
         if (tid < total) {
@@ -607,7 +677,7 @@ render_fwd_kernel(const __grid_constant__ Params<NF> p) {
         found += total;
         __syncthreads();
       }
-      if (first && tid == 0 && found != count) atomicOr(p.status, GF_FLAG_INTERNAL);
+      if (rb == 0 && cb == 0 && tid == 0 && found != count) atomicOr(p.status, GF_FLAG_INTERNAL);
 
       // Store the 32x32 sub-block.
       const float sc = p.cfg.out_scale;
@@ -794,21 +864,26 @@ __device__ __forceinline__ void fwd32_tile(const Params<NF>& p, int tg, bool ski
 #pragma unroll
   for (int i = 0; i < R / 2; ++i) V[i] = pk2(0.0f, 0.0f);
 
-  const Cands cd = tile_candidates(p, F, tr, tc);
+  // the tile's sorted list from the BIN stage; if the id buffer could not
+  // hold it, the ordered scan of every box of the field (same order)
+  const bool listed = count <= cap_left;
+  const int ncand = listed ? (int)count : F.K;
   int64_t found = 0;
-  for (int k0 = 0; k0 < cd.n && found < count; k0 += 32) {
-    const bool cv = k0 + lane < cd.n;
-    const int g = cv ? cd.at(k0 + lane) : 0;
+  for (int k0 = 0; k0 < ncand && found < count; k0 += 32) {
+    int g = 0;
     bool hit = false;
-    if (cv && GF_IN_BOUNDS(g < F.K && F.g_base + g < p.total_g)) {
-      const int4 b = box[g];
-      hit = (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
+    if (k0 + lane < ncand) {
+      if (listed) {
+        const int64_t v = ids[k0 + lane];
+        g = (int)v;
+        hit = v >= 0 && v < F.K;
+      } else if (GF_IN_BOUNDS(F.g_base + k0 + lane < p.total_g)) {
+        g = k0 + lane;
+        const int4 b = box[g];
+        hit = (b.x <= tr) & (tr <= b.y) & (b.z <= tc) & (tc <= b.w);
+      }
     }
     unsigned m = __ballot_sync(0xffffffffu, hit);
-    if (warp == 0 && hit && !(p.cfg.flags & kFlagIdsWritten)) {
-      const int64_t pos = found + __popc(m & ((1u << lane) - 1u));
-      if (pos < cap_left) ids[pos] = g;
-    }
     found += __popc(m);
     // Every hit's record is fetched by the lane that tested it, all lanes at
     // once, and handed to the warp by shuffles in ascending order: one load
@@ -1675,20 +1750,10 @@ gf_status fail(gf_status s, const char* fmt, ...) {
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Layout {
-  size_t hdr, records, boxes, goff, field_pairs, diff, slist, heavy, partials, total;
+  size_t hdr, records, boxes, goff, field_pairs, diff, cursor, heavy, partials, total;
   int64_t total_tiles, total_g, diff_ints, pair_cap;
-  int64_t slist_ints;  // forward: super-tile lists of the fields with K >= kListMinK (0 = none)
   int64_t heavy_items; // backward: capacity of the heavy-tile work items
-  int max_supertiles;
 };
-
-// Ints of a field's super-tile lists, or 0 when the field scans all K boxes.
-inline int64_t field_list_ints(int64_t out_f, int64_t in_f, int64_t k, const gf_config* cfg) {
-  if (k < kListMinK) return 0;
-  const int64_t ntr = (out_f + cfg->tile_out - 1) / cfg->tile_out, ntc = (in_f + cfg->tile_in - 1) / cfg->tile_in;
-  const int64_t ns = ((ntr + kSuperTile - 1) / kSuperTile) * ((ntc + kSuperTile - 1) / kSuperTile);
-  return ns * (k + 1);
-}
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
@@ -1757,18 +1822,6 @@ Layout layout(const gf_config* cfg, const gf_batch* batch, gf_pass pass) {
     const int64_t nd = (ntr + 1) * (ntc + 1);
     if (nd > kBinSmemCapInts) L.diff_ints += nd;
     if (!batch->ids) L.pair_cap += f.ids_capacity;
-    if (pass == GF_PASS_FORWARD) {
-      const int64_t li = field_list_ints(f.out_features, f.in_features, f.num_gaussians, cfg);
-      if (li > 0) {
-        L.slist_ints += li;
-        const int64_t ns = li / (f.num_gaussians + 1);
-        if (ns > L.max_supertiles) L.max_supertiles = (int)ns;
-      }
-    }
-  }
-  if (L.slist_ints > INT32_MAX) {  // beyond 32-bit list offsets: every field scans all its boxes
-    L.slist_ints = 0;
-    L.max_supertiles = 0;
   }
   if (batch->ids) L.pair_cap = batch->ids_capacity;
   size_t off = 0;
@@ -1778,7 +1831,8 @@ Layout layout(const gf_config* cfg, const gf_batch* batch, gf_pass pass) {
   L.goff = off; off = align256(off + 8 * (size_t)L.total_g);
   L.field_pairs = off; off = align256(off + 8 * (size_t)batch->num_fields);
   L.diff = off; off = align256(off + 4 * (size_t)L.diff_ints);
-  L.slist = off; off = align256(off + 4 * (size_t)L.slist_ints);
+  L.cursor = off;
+  if (pass == GF_PASS_FORWARD) off = align256(off + 4 * (size_t)L.total_tiles);
   L.heavy = off;
   if (pass == GF_PASS_FORWARD) {
     off = align256(off + 4 * (size_t)L.total_tiles);
@@ -1818,14 +1872,13 @@ void fill_params(Params<NF>& P, const gf_config* cfg, const gf_batch* batch, con
   P.goff = reinterpret_cast<int64_t*>(ws + L.goff);
   P.field_pairs = reinterpret_cast<int64_t*>(ws + L.field_pairs);
   P.diff = reinterpret_cast<int32_t*>(ws + L.diff);
-  P.slist = reinterpret_cast<int32_t*>(ws + L.slist);
+  P.cursor = reinterpret_cast<int32_t*>(ws + L.cursor);
   P.partials = reinterpret_cast<float4*>(ws + L.partials);
   P.part_cap = L.pair_cap;
   P.batch_ids = batch->ids;
   P.batch_cap = batch->ids_capacity;
   P.pair_base = batch->pair_base;
   int32_t tile_base = 0, g_base = 0, diff_base = 0;
-  int64_t slist_base = 0;
   int64_t part_base = 0;
   const size_t esz = cfg->out_dtype == GF_BF16 ? 2 : 4;
   for (int i = 0; i < batch->num_fields; ++i) {
@@ -1857,15 +1910,6 @@ void fill_params(Params<NF>& P, const gf_config* cfg, const gf_batch* batch, con
         ((reinterpret_cast<uintptr_t>(s.base_weight) & 15u) == 0) && (s.in_features % (int64_t)vec == 0) &&
         (cfg->tile_in % (int64_t)vec == 0))
       d.bits |= kFieldVecOk;
-    d.slist_base = 0;
-    if (L.slist_ints > 0) {
-      const int64_t li = field_list_ints(s.out_features, s.in_features, s.num_gaussians, cfg);
-      if (li > 0) {
-        d.bits |= kFieldLists;
-        d.slist_base = (int32_t)slist_base;
-        slist_base += li;
-      }
-    }
     const int64_t gvec = cfg->grad_dtype == GF_BF16 ? 8 : 4;
     if (((reinterpret_cast<uintptr_t>(s.grad_delta) & 15u) == 0) && (s.in_features % gvec == 0) &&
         (cfg->tile_in % gvec == 0))
@@ -1897,6 +1941,21 @@ cudaError_t allow_dynamic_smem(int bytes) {
   return e;
 }
 
+// The per-tile id lists of the BIN stage: pair emission, then the sorts.
+template <int NF>
+gf_status launch_tile_lists(const Params<NF>& p, const Layout& L, cudaStream_t st) {
+  if (L.total_g > 0) {
+    emit_pairs_kernel<NF><<<(int)ceil_div(L.total_g, kEmitWarps), 32 * kEmitWarps, 0, st>>>(p);
+    GF_LAUNCH_CHECK("emit_pairs_kernel");
+  }
+  sort_tiles_kernel<NF><<<(int)ceil_div(L.total_tiles, kSortWarps), 32 * kSortWarps, 0, st>>>(p);
+  GF_LAUNCH_CHECK("sort_tiles_kernel");
+  const int hg = L.total_tiles < kHeavyGridCap ? (int)L.total_tiles : kHeavyGridCap;
+  sort_heavy_kernel<NF><<<hg, kSortThreads, 0, st>>>(p);
+  GF_LAUNCH_CHECK("sort_heavy_kernel");
+  return GF_OK;
+}
+
 template <int NF>
 gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout& L, char* ws, cudaStream_t st,
                       unsigned stages = GF_STAGE_BIN | GF_STAGE_RENDER, int first_field = 0, int num_fields = -1) {
@@ -1922,20 +1981,11 @@ gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout&
       return fail(GF_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(cudaGetLastError()));
     bin_kernel<NF><<<p.n, kBinThreads, smem, st>>>(p, kBinSmemCapInts);
     GF_LAUNCH_CHECK("bin_kernel");
-    if (L.slist_ints > 0) {
-      super_list_kernel<NF><<<dim3((unsigned)ceil_div(L.max_supertiles, kListWarps), (unsigned)p.n), 32 * kListWarps, 0,
-                              st>>>(p);
-      GF_LAUNCH_CHECK("super_list_kernel");
-    }
-    if (!(stages & GF_STAGE_RENDER)) {
-      // the BIN stage alone also writes the id lists (the render normally does)
-      emit_ids_kernel<NF><<<(int)ceil_div(L.total_tiles, kEmitWarps), 32 * kEmitWarps, 0, st>>>(p);
-      GF_LAUNCH_CHECK("emit_ids_kernel");
-    }
+    const gf_status sl = launch_tile_lists(p, L, st);
+    if (sl != GF_OK) return sl;
     trace_mark(st);
   }
   if (!(stages & GF_STAGE_RENDER)) return GF_OK;
-  if (!(stages & GF_STAGE_BIN)) p.cfg.flags |= kFlagIdsWritten;
   NvtxRange r("gfield.render_fwd");
   const bool norm = p.cfg.normalize, clamp = p.cfg.has_clamp;
   int grid = (int)L.total_tiles;
@@ -2276,11 +2326,8 @@ gf_status noalloc_launch(Params<NF>& p, const gf_config* cfg, const gf_batch* ba
   if (e != cudaSuccess) return fail(GF_ERR_CUDA, "gf_forward_noalloc: %s", cudaGetErrorString(e));
   bin_kernel<NF><<<p.n, kBinThreads, sizeof(int) * (size_t)max_nd, st>>>(p, kBinSmemCapInts);
   GF_LAUNCH_CHECK("bin_kernel");
-  if (L.slist_ints > 0) {
-    super_list_kernel<NF><<<dim3((unsigned)ceil_div(L.max_supertiles, kListWarps), (unsigned)p.n), 32 * kListWarps, 0,
-                            st>>>(p);
-    GF_LAUNCH_CHECK("super_list_kernel");
-  }
+  const gf_status sl = launch_tile_lists(p, L, st);
+  if (sl != GF_OK) return sl;
   const bool norm = p.cfg.normalize, clamp = p.cfg.has_clamp;
   const int grid = (int)L.total_tiles;
 #define GF_FWD(N, C, O)                                                                         \

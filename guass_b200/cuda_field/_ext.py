@@ -181,6 +181,7 @@ class GaussianFieldExtension:
         gdt = _lib.GF_BF16 if out_dtype == torch.bfloat16 else _lib.GF_F32
         cfg = make_config(tile_out, tile_in, sigma_multiplier, normalize, clamp_quad, out_dtype=gdt,
                           out_scale=out_scale)
+        retried = False
         while True:
             ids = torch.empty(max(cap, 1), dtype=torch.int64, device=device)
             field = _lib.GfField(out_features=out_f, in_features=in_f, num_gaussians=k,
@@ -204,9 +205,10 @@ class GaussianFieldExtension:
             if num_pairs <= cap:
                 break
             cap = num_pairs  # rare: re-render with an exact buffer
+            retried = True
         self._pairs_hint[key] = num_pairs
-        if _VALIDATE:
-            raise_device_flags(ws)
+        if _VALIDATE:  # (a first attempt that outgrew its id buffer left the capacity bit)
+            raise_device_flags(ws, ignore=_lib.GF_FLAG_CAPACITY if retried else 0)
         return delta, tile_ptr, ids[:num_pairs]
 
     # ext.cpp:38-72, field_impl.cu:165-179
