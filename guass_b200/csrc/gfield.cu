@@ -306,8 +306,54 @@ __device__ __forceinline__ int64_t block_exclusive_scan(int64_t v, int64_t* s_wa
   return before + x - v;
 }
 
+// Lower bound of the scaled form q' = -0.5*quad at one tile corner, minus
+// the evaluation-error margin (h* are the -0.5-scaled inverse entries).
+__device__ __forceinline__ float corner_bound(float dx, float dy, float h00, float h01, float h11) {
+  const float q = dx * (h00 * dx + h01 * dy) + dy * (h01 * dx + h11 * dy);
+  const float s = fabsf(h00) * dx * dx + 2.0f * fabsf(h01) * fabsf(dx * dy) + fabsf(h11) * dy * dy;
+  return q - 1e-5f * s;
+}
+
 // ---------------------------------------------------------------------------
-// Forward kernel 1: preprocess + stable binning, one CTA per field.
+// Kernel 0 of both passes: per-Gaussian preprocess (forward.cu:134-209; the
+// reference's backward rebuilds it too, backward.cu:552-557), one thread per
+// Gaussian of every field: the render record and the tile box.
+constexpr int kGeoThreads = 256;
+
+//
+// Backward (CLAMP_FLAG): may any element of any of the Gaussian's tiles reach
+// the clamp?  The form is convex, so over the rectangle of its tile-aligned
+// box it is largest at a corner -- with monotonic axes the rectangle is
+// spanned by the end rows and columns (bwd_prep_kernel checks the axes and
+// flags every Gaussian of a field whose axes are not).  The answer travels as
+// the sign of the record's (positive) normalisation factor: negative = test
+// per tile.
+template <int NF, bool CLAMP_FLAG>
+__global__ void __launch_bounds__(kGeoThreads) geometry_kernel(const __grid_constant__ Params<NF> p) {
+  const int G = blockIdx.x * kGeoThreads + threadIdx.x;
+  if (G >= p.total_g) return;
+  const int fi = field_of_gaussian(p, G);
+  const DevField& F = p.f[fi];
+  const int g = G - F.g_base;
+  const float mu_r = F.mu[2 * g], mu_c = F.mu[2 * g + 1];
+  const Geo geo = geometry(mu_r, mu_c, F.chol[3 * g], F.chol[3 * g + 1], F.chol[3 * g + 2], F, p.cfg);
+  float4* rec = p.records + 2 * (size_t)G;
+  store_record(rec, mu_r, mu_c, F.amp[g], geo);
+  p.boxes[G] = geo.box;
+  if (CLAMP_FLAG && p.cfg.has_clamp) {
+    const int4 box = geo.box;
+    const int ra = box.x * p.cfg.tile_out, rb = min((box.y + 1) * p.cfg.tile_out, F.out_f) - 1;
+    const int ca = box.z * p.cfg.tile_in, cb = min((box.w + 1) * p.cfg.tile_in, F.in_f) - 1;
+    const float h00 = -0.5f * geo.i00, h01 = -0.5f * geo.i01, h11 = -0.5f * geo.i11;
+    const float x0 = F.row[ra] - mu_r, x1 = F.row[rb] - mu_r, y0 = F.col[ca] - mu_c, y1 = F.col[cb] - mu_c;
+    const float lo = fminf(fminf(corner_bound(x0, y0, h00, h01, h11), corner_bound(x0, y1, h00, h01, h11)),
+                           fminf(corner_bound(x1, y0, h00, h01, h11), corner_bound(x1, y1, h00, h01, h11)));
+    if (!(lo > p.cfg.nclamp)) rec[0].w = -rec[0].w;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Forward kernel 1: stable binning counts, one CTA per field.
 //
 // Each Gaussian's tile box adds +1/-1 at its four corners of a
 // (ntr+1) x (ntc+1) difference array; a 2-D prefix sum gives every tile's
@@ -330,15 +376,12 @@ bin_kernel(const __grid_constant__ Params<NF> p, int smem_cap_ints) {
   int* D = (nd <= smem_cap_ints) ? s_dyn : (p.diff + F.diff_base);
   for (int i = tid; i < nd; i += bs) D[i] = 0;
   __syncthreads();
-  for (int g = tid; g < F.K; g += bs) {
-    const float mu_r = F.mu[2 * g], mu_c = F.mu[2 * g + 1];
-    const Geo geo = geometry(mu_r, mu_c, F.chol[3 * g], F.chol[3 * g + 1], F.chol[3 * g + 2], F, p.cfg);
-    store_record(p.records + 2 * (size_t)(F.g_base + g), mu_r, mu_c, F.amp[g], geo);
-    p.boxes[F.g_base + g] = geo.box;
-    atomicAdd(&D[geo.box.x * W + geo.box.z], 1);
-    atomicAdd(&D[geo.box.x * W + geo.box.w + 1], -1);
-    atomicAdd(&D[(geo.box.y + 1) * W + geo.box.z], -1);
-    atomicAdd(&D[(geo.box.y + 1) * W + geo.box.w + 1], 1);
+  for (int g = tid; g < F.K; g += bs) {  // boxes from geometry_kernel
+    const int4 b = p.boxes[F.g_base + g];
+    atomicAdd(&D[b.x * W + b.z], 1);
+    atomicAdd(&D[b.x * W + b.w + 1], -1);
+    atomicAdd(&D[(b.y + 1) * W + b.z], -1);
+    atomicAdd(&D[(b.y + 1) * W + b.w + 1], 1);
   }
   __syncthreads();
   for (int r = tid; r < H; r += bs) {
@@ -520,7 +563,25 @@ __global__ void __launch_bounds__(32 * kSortWarps) sort_tiles_kernel(const __gri
   const TileIds<NF> L = tile_ids(p, fi, tg - p.f[fi].tile_base);
   const int n0 = (int)L.count;
   if (n0 <= 1 || n0 > kHeavyPairs || !L.complete()) return;
-  int n = 32;
+  if (n0 <= 32) {
+    // one id per lane: leave a list that is already ascending alone, else a
+    // bitonic sort across the lanes (the sort network on register values)
+    int32_t v = lane < n0 ? (int32_t)L.ids[lane] : INT32_MAX;
+    const int32_t prev = __shfl_up_sync(0xffffffffu, v, 1);
+    if (__ballot_sync(0xffffffffu, lane > 0 && lane < n0 && prev > v) == 0u) return;
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        const int32_t o = __shfl_xor_sync(0xffffffffu, v, j);
+        const bool lower = (lane & j) == 0, up = (lane & k) == 0;
+        v = (lower == up) ? min(v, o) : max(v, o);
+      }
+    }
+    if (lane < n0) L.ids[lane] = v;
+    return;
+  }
+  int n = 64;
   while (n < n0) n <<= 1;
   int32_t* s = s_keys[warp];
   for (int i = lane; i < n; i += 32) s[i] = i < n0 ? (int32_t)L.ids[i] : INT32_MAX;
@@ -1065,17 +1126,9 @@ __global__ void __launch_bounds__(32 * kHeavyWarps) render_fwd32_heavy_kernel(co
   }
 }
 
-// Lower bound of the scaled form q' = -0.5*quad at one tile corner, minus
-// the evaluation-error margin (h* are the -0.5-scaled inverse entries).
-__device__ __forceinline__ float corner_bound(float dx, float dy, float h00, float h01, float h11) {
-  const float q = dx * (h00 * dx + h01 * dy) + dy * (h01 * dx + h11 * dy);
-  const float s = fabsf(h00) * dx * dx + 2.0f * fabsf(h01) * fabsf(dx * dy) + fabsf(h11) * dy * dy;
-  return q - 1e-5f * s;
-}
-
 // ---------------------------------------------------------------------------
-// Backward kernel 1: per-field preprocess (backward.cu:552-557 rebuilds the
-// geometry too), plus each Gaussian's first slot in the pair-partial buffer:
+// Backward kernel 1: per field, after geometry_kernel, each Gaussian's first
+// slot in the pair-partial buffer:
 // an exclusive scan of tiles_touched, i.e. the reference's pair emission
 // order (forward.cu:211-241).  Also checks that the saved pair count matches.
 template <int NF>
@@ -1086,7 +1139,8 @@ bwd_prep_kernel(const __grid_constant__ Params<NF> p) {
   const DevField& F = p.f[fi];
   const int tid = threadIdx.x, bs = blockDim.x;
   // Are the axes monotonic?  Then the coordinates of any range of rows (or
-  // columns) lie between the range's end values, which the clamp bounds use.
+  // columns) lie between the range's end values, which geometry_kernel's
+  // clamp bounds use.
   bool mono = true;
   if (p.cfg.has_clamp) {
     bool up_r = true, dn_r = true, up_c = true, dn_c = true;
@@ -1105,30 +1159,13 @@ bwd_prep_kernel(const __grid_constant__ Params<NF> p) {
   const int per = (F.K + bs - 1) / bs;
   const int g0 = min(F.K, tid * per), g1 = min(F.K, g0 + per);
   int64_t local = 0;
-  for (int g = g0; g < g1; ++g) {
-    const float mu_r = F.mu[2 * g], mu_c = F.mu[2 * g + 1];
-    const Geo geo = geometry(mu_r, mu_c, F.chol[3 * g], F.chol[3 * g + 1], F.chol[3 * g + 2], F, p.cfg);
-    float4* rec = p.records + 2 * (size_t)(F.g_base + g);
-    store_record(rec, mu_r, mu_c, F.amp[g], geo);
-    if (p.cfg.has_clamp) {
-      // May any element of any of this Gaussian's tiles reach the clamp?  The
-      // form is convex, so over the rectangle of its tile-aligned box it is
-      // largest at a corner.  The answer travels as the sign of the record's
-      // (positive) normalisation factor: negative = test per tile.
-      bool may = true;
-      if (mono) {
-        const int ra = geo.box.x * p.cfg.tile_out, rb = min((geo.box.y + 1) * p.cfg.tile_out, F.out_f) - 1;
-        const int ca = geo.box.z * p.cfg.tile_in, cb = min((geo.box.w + 1) * p.cfg.tile_in, F.in_f) - 1;
-        const float h00 = -0.5f * geo.i00, h01 = -0.5f * geo.i01, h11 = -0.5f * geo.i11;
-        const float x0 = F.row[ra] - mu_r, x1 = F.row[rb] - mu_r, y0 = F.col[ca] - mu_c, y1 = F.col[cb] - mu_c;
-        const float lo = fminf(fminf(corner_bound(x0, y0, h00, h01, h11), corner_bound(x0, y1, h00, h01, h11)),
-                               fminf(corner_bound(x1, y0, h00, h01, h11), corner_bound(x1, y1, h00, h01, h11)));
-        may = !(lo > p.cfg.nclamp);
-      }
-      if (may) rec[0].w = -rec[0].w;
+  for (int g = g0; g < g1; ++g) {  // boxes from geometry_kernel
+    const int4 box = p.boxes[F.g_base + g];
+    if (!mono) {  // the clamp test of geometry_kernel assumed monotonic axes: test every tile
+      float4* rec = p.records + 2 * (size_t)(F.g_base + g);
+      rec[0].w = -fabsf(rec[0].w);
     }
-    p.boxes[F.g_base + g] = geo.box;
-    local += (int64_t)(geo.box.y - geo.box.x + 1) * (geo.box.w - geo.box.z + 1);
+    local += (int64_t)(box.y - box.x + 1) * (box.w - box.z + 1);
   }
   int64_t total;
   int64_t off = block_exclusive_scan(local, s_warp, &total);
@@ -1979,6 +2016,10 @@ gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout&
     trace_mark(st);
     if (cudaMemsetAsync(p.heavy_count, 0, sizeof(uint32_t), st) != cudaSuccess)
       return fail(GF_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(cudaGetLastError()));
+    if (L.total_g > 0) {
+      geometry_kernel<NF, false><<<(int)ceil_div(L.total_g, kGeoThreads), kGeoThreads, 0, st>>>(p);
+      GF_LAUNCH_CHECK("geometry_kernel");
+    }
     bin_kernel<NF><<<p.n, kBinThreads, smem, st>>>(p, kBinSmemCapInts);
     GF_LAUNCH_CHECK("bin_kernel");
     const gf_status sl = launch_tile_lists(p, L, st);
@@ -2059,6 +2100,10 @@ gf_status run_backward(const gf_config* cfg, const gf_batch* batch, const Layout
     trace_mark(st);
     if (cudaMemsetAsync(p.heavy_count, 0, sizeof(uint32_t), st) != cudaSuccess)
       return fail(GF_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(cudaGetLastError()));
+    if (L.total_g > 0) {
+      geometry_kernel<NF, true><<<(int)ceil_div(L.total_g, kGeoThreads), kGeoThreads, 0, st>>>(p);
+      GF_LAUNCH_CHECK("geometry_kernel");
+    }
     bwd_prep_kernel<NF><<<p.n, kBinThreads, 0, st>>>(p);
     GF_LAUNCH_CHECK("bwd_prep_kernel");
     trace_mark(st);
@@ -2324,6 +2369,10 @@ gf_status noalloc_launch(Params<NF>& p, const gf_config* cfg, const gf_batch* ba
   cudaError_t e = cudaFuncSetAttribute(bin_kernel<NF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        kBinSmemCapInts * 4);
   if (e != cudaSuccess) return fail(GF_ERR_CUDA, "gf_forward_noalloc: %s", cudaGetErrorString(e));
+  if (L.total_g > 0) {
+    geometry_kernel<NF, false><<<(int)ceil_div(L.total_g, kGeoThreads), kGeoThreads, 0, st>>>(p);
+    GF_LAUNCH_CHECK("geometry_kernel");
+  }
   bin_kernel<NF><<<p.n, kBinThreads, sizeof(int) * (size_t)max_nd, st>>>(p, kBinSmemCapInts);
   GF_LAUNCH_CHECK("bin_kernel");
   const gf_status sl = launch_tile_lists(p, L, st);
