@@ -47,6 +47,90 @@ def _capacity_kw(shapes, tile_out, tile_in):
     return ({"ids_capacity": max(bound, 1)}, False) if bound <= MAX_BOUND_PAIRS else ({}, True)
 
 
+class _PendingNorms:
+    """Per-module norms on their way to the host: a non-blocking copy into
+    pinned memory and an event; :meth:`get` waits for the event once."""
+
+    def __init__(self, norms: torch.Tensor):
+        if norms.is_cuda:
+            self._host = torch.empty(norms.shape, dtype=norms.dtype, pin_memory=True)
+            self._host.copy_(norms, non_blocking=True)
+            self._event = torch.cuda.Event()
+            self._event.record()
+        else:
+            self._host, self._event = norms, None
+        self._values = None
+
+    def get(self, f: int) -> float:
+        if self._values is None:
+            if self._event is not None:
+                self._event.synchronize()
+            self._values = self._host.tolist()
+        return self._values[f]
+
+
+class _LayerMetadata(dict):
+    """A layer's ``last_forward_metadata`` whose ``delta_w_norm`` (a float, as
+    the layer stores it) is read from :class:`_PendingNorms` on first access
+    of any entry; afterwards it is a plain dict."""
+
+    def __init__(self, base: dict, norms: _PendingNorms, f: int):
+        super().__init__(base)
+        self._pending = (norms, f)
+
+    def _resolve(self):
+        if self._pending is not None:
+            norms, f = self._pending
+            self._pending = None
+            dict.__setitem__(self, "delta_w_norm", float(norms.get(f)))
+
+    def __getitem__(self, key):
+        self._resolve()
+        return dict.__getitem__(self, key)
+
+    def get(self, key, default=None):
+        self._resolve()
+        return dict.get(self, key, default)
+
+    def __contains__(self, key):
+        self._resolve()
+        return dict.__contains__(self, key)
+
+    def __iter__(self):
+        self._resolve()
+        return dict.__iter__(self)
+
+    def __len__(self):
+        self._resolve()
+        return dict.__len__(self)
+
+    def __eq__(self, other):
+        self._resolve()
+        return dict.__eq__(self, other)
+
+    __hash__ = None
+
+    def __repr__(self):
+        self._resolve()
+        return dict.__repr__(self)
+
+    def keys(self):
+        self._resolve()
+        return dict.keys(self)
+
+    def values(self):
+        self._resolve()
+        return dict.values(self)
+
+    def items(self):
+        self._resolve()
+        return dict.items(self)
+
+    def copy(self):
+        self._resolve()
+        return dict(dict.items(self))
+
+
 class BatchedFieldFunction(torch.autograd.Function):
     """Packed render of every field of ``batch``.
 
@@ -234,9 +318,13 @@ class BatchedAdapters:
         packed = BatchedFieldFunction.apply(self.batch, mu, chol, amp)
         if self.track_metadata:
             self._publish_metadata(packed.detach())
+        # one split, not a slice per module: the backward of split_with_sizes is
+        # a single concatenation of the modules' gradients, while every slice's
+        # backward materialises a zero-filled gradient of the whole packed delta
+        sizes = [self.n_off[f + 1] - self.n_off[f] for f in range(len(self.modules))]
         out = []
-        for f, m in enumerate(self.modules):
-            d = packed[self.n_off[f]:self.n_off[f + 1]].view(m.out_features, m.in_features)
+        for part, m in zip(torch.split(packed, sizes), self.modules):
+            d = part.view(m.out_features, m.in_features)
             scale = m.adapter_config.adapter_scale
             out.append(d * scale if scale != 1.0 and not self.fused else d)
         self._current = out
@@ -247,23 +335,22 @@ class BatchedAdapters:
         writes (gaussian_linear.py:196-219) and GUASS's diagnostics read
         (utils/logging.py:17-62): execution_mode, accumulate_backend and
         delta_w_norm (of the unscaled delta, as the layer computes it).  The
-        norms of all layers come from one fused launch and one host read (the
-        layer itself reads one per layer); the fused mode renders W0 + delta
-        and reports no norm."""
+        norms of all layers come from one fused launch and one asynchronous
+        copy to pinned host memory; the render does not wait for them: the
+        first read of a module's metadata waits for that copy (the layer
+        itself synchronises once per layer per forward).  The fused mode
+        renders W0 + delta and reports no norm."""
         meta = {"execution_mode": "cuda_field_train", "accumulate_backend": "gfield_batched"}
-        norms = [None] * len(self.modules)
+        norms = None
         if not self.fused:
-            views = [packed[self.n_off[f]:self.n_off[f + 1]] for f in range(len(self.modules))]
+            views = torch.split(packed, [self.n_off[f + 1] - self.n_off[f] for f in range(len(self.modules))])
             try:
                 parts = torch._foreach_norm(views, 2, dtype=torch.float32)  # one fused launch
             except (RuntimeError, TypeError):
                 parts = [torch.linalg.vector_norm(v, dtype=torch.float32) for v in views]
-            norms = torch.stack(list(parts)).tolist()
-        for m, n in zip(self.modules, norms):
-            md = dict(meta)
-            if n is not None:
-                md["delta_w_norm"] = float(n)
-            m.last_forward_metadata = md
+            norms = _PendingNorms(torch.stack(list(parts)))
+        for f, m in enumerate(self.modules):
+            m.last_forward_metadata = _LayerMetadata(meta, norms, f) if norms is not None else dict(meta)
 
     def _slot(self, f):
         if self._current is None:

@@ -347,3 +347,21 @@ def test_each_render_returns_its_own_delta():
     for a, b, c in zip(first, kept, second):
         assert torch.equal(a.detach(), b)
         assert not torch.equal(c.detach(), b)
+
+
+def test_layer_metadata_resolves_norm_on_read():
+    """The deferred delta_w_norm reads like the layer's plain dict: get(),
+    dict() copies, ** unpacking and item access all see a float."""
+    from guass_b200.adapters import _LayerMetadata, _PendingNorms
+
+    norms = _PendingNorms(torch.tensor([1.5, 2.5]))
+    base = {"execution_mode": "cuda_field_train"}
+    for f, want in ((0, 1.5), (1, 2.5)):
+        for read in (lambda m: m.get("delta_w_norm"), lambda m: dict(m)["delta_w_norm"],
+                     lambda m: {**m}["delta_w_norm"], lambda m: m["delta_w_norm"],
+                     lambda m: dict(m.items())["delta_w_norm"]):
+            md = _LayerMetadata(base, norms, f)
+            v = read(md)
+            assert isinstance(v, float) and v == want
+        md = _LayerMetadata(base, norms, f)
+        assert len(md) == 2 and "delta_w_norm" in md and md == {**base, "delta_w_norm": want}
