@@ -369,23 +369,47 @@ def run_e2e_model(w: UNetWorkload, steps: int, warmup: int, world: int, mode: st
     else:
         ModelRenderer(model, out_dtype=torch.bfloat16)
     params = [p for m in layers for p in (m.mu_raw, m.chol_raw, m.amp)]
-    h_params = [p.detach().cpu().pin_memory() for p in params]
-    h_grads = [w.fields[i].grad.view(w.fields[i].out_features, w.fields[i].in_features).pin_memory() for i in w.own]
-    d_grads = [g.cuda() for g in h_grads]
-    h_out = [torch.empty(p.shape, dtype=p.dtype).pin_memory() for p in params]
-    h2d = sum(t.numel() * t.element_size() for t in h_params + h_grads)
-    d2h = sum(t.numel() * t.element_size() for t in h_out)
+    # dL/d(delta) in the dtype autograd hands each layer's delta (bf16 under
+    # ModelRenderer, fp32 from the per-layer drop-in)
+    with torch.no_grad():
+        delta_dtype = model()[0].dtype
+
+    def flat(tensors, dtype, pinned):
+        n = sum(t.numel() for t in tensors)
+        buf = torch.empty(n, dtype=dtype, pin_memory=True) if pinned else torch.empty(n, dtype=dtype, device="cuda")
+        views, o = [], 0
+        for t in tensors:
+            views.append(buf[o:o + t.numel()].view(t.shape))
+            o += t.numel()
+        return buf, views
+
+    # one pinned staging buffer per direction: three copies per step instead of
+    # one per tensor (the layers' parameters stay separate nn.Parameters)
+    h_params, h_pviews = flat(params, torch.float32, True)
+    d_params, d_pviews = flat(params, torch.float32, False)
+    for hv, p in zip(h_pviews, params):
+        hv.copy_(p.detach().cpu())
+    grads_src = [w.fields[i].grad.view(w.fields[i].out_features, w.fields[i].in_features) for i in w.own]
+    h_grads, h_gviews = flat(grads_src, delta_dtype, True)
+    for hv, g in zip(h_gviews, grads_src):
+        hv.copy_(g)
+    d_grads, d_gviews = flat(grads_src, delta_dtype, False)
+    h_out, _ = flat(params, torch.float32, True)
+    d_out, d_oviews = flat(params, torch.float32, False)
+    h2d = h_params.numel() * 4 + h_grads.numel() * h_grads.element_size()
+    d2h = h_out.numel() * 4
 
     def step():
         with torch.no_grad():
-            for p, h in zip(params, h_params):
-                p.copy_(h, non_blocking=True)
-            for d, h in zip(d_grads, h_grads):
-                d.copy_(h, non_blocking=True)
+            d_params.copy_(h_params, non_blocking=True)
+            torch._foreach_copy_(params, d_pviews)
+            d_grads.copy_(h_grads, non_blocking=True)
         deltas = model()
-        torch.autograd.backward(deltas, [g.to(d.dtype) for d, g in zip(deltas, d_grads)])
-        for p, h in zip(params, h_out):
-            h.copy_(p.grad, non_blocking=True)
+        torch.autograd.backward(deltas, d_gviews)
+        with torch.no_grad():
+            torch._foreach_copy_(d_oviews, [p.grad for p in params])
+            h_out.copy_(d_out, non_blocking=True)
+        for p in params:
             p.grad = None
 
     for _ in range(warmup):
@@ -988,7 +1012,8 @@ def main():
                              "pattern), fp32 delta" if mode == "dropin" else
                              "GUASS layer API with adapters.ModelRenderer: one batched render per model forward "
                              "(bf16 delta), one batched backward") +
-                            "; layer params and dL/d(delta) H2D from pinned memory, gradients D2H, every step"}
+                            "; layer params and dL/d(delta) (in the delta's dtype) H2D from one pinned staging "
+                            "buffer each, gradients D2H through one, every step"}
             except Exception as exc:  # noqa: BLE001
                 e2e_layer[key] = {"error": f"{type(exc).__name__}: {exc}"}
 
