@@ -964,6 +964,11 @@ __device__ __forceinline__ void fwd32_tile(const Params<NF>& p, int tg, bool ski
       const float o00 = rh.x * kLog2e, o01 = 2.0f * (rh.y * kLog2e), o11 = rh.z * kLog2e;
       const float oamp = NORM ? ra.z * ra.w : ra.z;
       const float nclamp2 = nclamp * kLog2e;
+      // As in the base-2 backward, a clamp at quad >= 64 is not applied: the
+      // clamp only raises a term beyond it to amp * e^(-clamp/2), so leaving
+      // it out changes an element by less than |amp| * e^-32 = 1.3e-14 |amp|
+      // per Gaussian, in absolute terms.
+      const bool clamp_terms = CLAMP && nclamp > -32.0f;
       while (m) {
         const int src = __ffs(m) - 1;
         m &= m - 1;
@@ -974,16 +979,22 @@ __device__ __forceinline__ void fwd32_tile(const Params<NF>& p, int tg, bool ski
         const float b1 = g01x2 * dy, c0 = g11 * dy * dy;
         const f2 G00 = pk2(g00, g00), B1 = pk2(b1, b1), C0 = pk2(c0, c0), MUR = pk2(mur, mur);
         const f2 AMP = pk2(ampn, ampn);
+        if (clamp_terms) {
 #pragma unroll
-        for (int i = 0; i < R / 2; ++i) {
-          const f2 DX = sub2(CR[i], MUR);
-          f2 Q = fma2(DX, fma2(G00, DX, B1), C0);
-          if (CLAMP) {
+          for (int i = 0; i < R / 2; ++i) {
+            const f2 DX = sub2(CR[i], MUR);
+            f2 Q = fma2(DX, fma2(G00, DX, B1), C0);
             float q0, q1;
             up2(Q, q0, q1);
             Q = pk2(fmaxf(q0, nclamp2), fmaxf(q1, nclamp2));
+            V[i] = fma2(AMP, ex2_2(Q), V[i]);
           }
-          V[i] = fma2(AMP, ex2_2(Q), V[i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < R / 2; ++i) {
+            const f2 DX = sub2(CR[i], MUR);
+            V[i] = fma2(AMP, ex2_2(fma2(DX, fma2(G00, DX, B1), C0)), V[i]);
+          }
         }
       }
     } else {
@@ -1378,7 +1389,7 @@ render_bwd_kernel(const __grid_constant__ Params<NF> p) {
 // runs.  Results are identical either way.  The next pair's id, box and record
 // are loaded while the current pair computes.
 #ifndef GF_BWD32_WARPS
-#define GF_BWD32_WARPS 4
+#define GF_BWD32_WARPS 2
 #endif
 // row stride of the transposed dL/d(delta) tile: 36 floats keeps every
 // column 16-byte aligned and the lanes' 128-bit reads conflict-free
@@ -1398,11 +1409,13 @@ struct PairSums {
 // uses CUDA's expf, which the bit parity of delta requires.
 __device__ __forceinline__ float exp_via_ex2(float q) { return ex2_approx(__fmul_rn(q, kLog2e)); }
 
-// One row pair (rows 2k, 2k+1 in the two halves of R2, their dL/d(delta) in G2).
+// One row pair (rows 2k, 2k+1 in the two halves of each argument): the row
+// terms DX = row - mu_r, P0 = round(h00 * DX) and P1 = round(h01 * DX) (the
+// same for every lane, computed once per row by bwd32_pairs) and the rows'
+// dL/d(delta) G2 of this lane's column.
 template <bool NORM, bool TRACK_CLAMP, bool EX2>
-__device__ __forceinline__ void bwd32_row_pair(PairSums& S, f2 R2, f2 G2, f2 H00, f2 H01, f2 H11, f2 A01, f2 A11,
-                                               f2 DY, f2 MUR, float nclamp, float nf) {
-  const f2 DX = sub2(R2, MUR);
+__device__ __forceinline__ void bwd32_row_pair(PairSums& S, f2 DX, f2 P0, f2 P1, f2 G2, f2 H00, f2 H01, f2 H11,
+                                               f2 A01, f2 A11, f2 DY, float nclamp, float nf) {
   const f2 T1 = fma2(H00, DX, A01);
   const f2 T2 = fma2(H01, DX, A11);
   const f2 Q = fma2(DX, T1, mul2(DY, T2));
@@ -1448,63 +1461,88 @@ __device__ __forceinline__ void bwd32_row_pair(PairSums& S, f2 R2, f2 G2, f2 H00
   S.U1 = fma2(GBA, DX, S.U1);
   S.U2 = fma2(mul2(GBA, DX), DX, S.U2);
   // per-element mu factors with the reference's roundings (see render_bwd_kernel)
-  S.M0 = fma2(GBA, fma2(H01, DY, mul2(H00, DX)), S.M0);
-  S.M1 = fma2(GBA, fma2(H11, DY, mul2(H01, DX)), S.M1);
+  S.M0 = fma2(GBA, fma2(H01, DY, P0), S.M0);
+  S.M1 = fma2(GBA, fma2(H11, DY, P1), S.M1);
 }
 
-// Sum over the 32 rows of one lane's column for one pair: rows and the
-// column's dL/d(delta) come from shared memory four at a time (128-bit loads;
-// the row vector is a broadcast, the column is this lane's own).
+// Sum over the 32 rows of one lane's column for one pair: the row terms
+// (s_rt: DX[32], P0[32], P1[32] of this warp) and the column's dL/d(delta)
+// come from shared memory four rows at a time (128-bit loads; the row terms
+// are broadcasts, the column is this lane's own).
 template <bool NORM, bool TRACK_CLAMP, bool EX2>
-__device__ __forceinline__ PairSums bwd32_pair_rows(const float* s_rows, const float* s_gcol, f2 H00, f2 H01,
-                                                   f2 H11, f2 A01, f2 A11, f2 DY, f2 MUR, float nclamp, float nf) {
+__device__ __forceinline__ PairSums bwd32_pair_rows(const float* s_rt, const float* s_gcol, f2 H00, f2 H01,
+                                                   f2 H11, f2 A01, f2 A11, f2 DY, float nclamp, float nf) {
   const f2 zero2 = pk2(0.0f, 0.0f);
   PairSums S{zero2, zero2, zero2, zero2, zero2, zero2};
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    const float4 rr = *reinterpret_cast<const float4*>(&s_rows[4 * k]);
+    const float4 dx = *reinterpret_cast<const float4*>(&s_rt[4 * k]);
+    const float4 p0 = *reinterpret_cast<const float4*>(&s_rt[32 + 4 * k]);
+    const float4 p1 = *reinterpret_cast<const float4*>(&s_rt[64 + 4 * k]);
     const float4 gg = *reinterpret_cast<const float4*>(&s_gcol[4 * k]);
-    bwd32_row_pair<NORM, TRACK_CLAMP, EX2>(S, pk2(rr.x, rr.y), pk2(gg.x, gg.y), H00, H01, H11, A01, A11, DY, MUR,
-                                           nclamp, nf);
-    bwd32_row_pair<NORM, TRACK_CLAMP, EX2>(S, pk2(rr.z, rr.w), pk2(gg.z, gg.w), H00, H01, H11, A01, A11, DY, MUR,
-                                           nclamp, nf);
+    bwd32_row_pair<NORM, TRACK_CLAMP, EX2>(S, pk2(dx.x, dx.y), pk2(p0.x, p0.y), pk2(p1.x, p1.y), pk2(gg.x, gg.y),
+                                           H00, H01, H11, A01, A11, DY, nclamp, nf);
+    bwd32_row_pair<NORM, TRACK_CLAMP, EX2>(S, pk2(dx.z, dx.w), pk2(p0.z, p0.w), pk2(p1.z, p1.w), pk2(gg.z, gg.w),
+                                           H00, H01, H11, A01, A11, DY, nclamp, nf);
   }
   if (!TRACK_CLAMP) S.T0 = S.U0;
   return S;
 }
 
-template <int NF, bool NORM, bool CLAMP, int GT, bool EX2>
-__device__ __forceinline__ void bwd32_tile(const Params<NF>& p, int tg, int pair_lo, int pair_hi, bool skip_heavy,
-                                           float* s_rows, float* s_gt) {
-  const int fi = field_of_tile(p, tg);
-  const DevField& F = p.f[fi];
+// One tile's work in the 32x32 backward: its field, position, pair range in
+// the id list and whether its dL/d(delta) block can be staged with 16-byte
+// copies.  False when the tile has nothing to do here (no pairs, a heavy tile
+// left to render_bwd32_heavy_kernel, or inconsistent saved state, which
+// raises GF_FLAG_STATE).  Every thread of the CTA computes the same job.
+struct Bwd32Job {
+  int fi, tr, tc, th, tw, count;
+  int64_t start, id_base;
+  bool vec;
+};
+
+template <int NF>
+__device__ __forceinline__ bool bwd32_job(const Params<NF>& p, int tg, bool skip_heavy, Bwd32Job& j) {
+  j.fi = field_of_tile(p, tg);
+  const DevField& F = p.f[j.fi];
   const int t = tg - F.tile_base;
-  const int tr = t / F.ntc, tc = t % F.ntc;
-  const int64_t start = F.tile_ptr[t];
-  const int64_t count64 = F.tile_ptr[t + 1] - start;
-  if (count64 <= 0) return;
-  const int64_t id_base = (p.batch_ids != nullptr) ? p.pair_base[fi] : 0;
+  j.tr = t / F.ntc;
+  j.tc = t % F.ntc;
+  j.start = F.tile_ptr[t];
+  const int64_t count64 = F.tile_ptr[t + 1] - j.start;
+  if (count64 <= 0) return false;
+  j.id_base = (p.batch_ids != nullptr) ? p.pair_base[j.fi] : 0;
   const int64_t id_limit = (p.batch_ids != nullptr) ? p.batch_cap : F.ids_cap;
   // a tile holds at most K pairs (one per Gaussian), K < 2^30
-  if (start < 0 || id_base < 0 || id_base + start + count64 > id_limit || count64 > F.K) {
+  if (j.start < 0 || j.id_base < 0 || j.id_base + j.start + count64 > id_limit || count64 > F.K) {
     if (threadIdx.x == 0) atomicOr(p.status, GF_FLAG_STATE);
-    return;
+    return false;
   }
-  const int count = (int)count64;
-  if (skip_heavy && count > kHeavyPairs) return;  // chunks of it go to render_bwd32_heavy_kernel
-  const int lo = pair_lo, hi = min(pair_hi, count);
-  if (lo >= hi) return;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int row0 = tr * 32, col0 = tc * 32;
-  const int th = min(32, F.out_f - row0), tw = min(32, F.in_f - col0);
+  j.count = (int)count64;
+  if (skip_heavy && j.count > kHeavyPairs) return false;  // chunks of it go to render_bwd32_heavy_kernel
+  const int row0 = j.tr * 32, col0 = j.tc * 32;
+  j.th = min(32, F.out_f - row0);
+  j.tw = min(32, F.in_f - col0);
+  const size_t gbase = (size_t)row0 * F.in_f + col0;
+  j.vec = j.th == 32 && j.tw == 32 && (F.bits & kFieldGradVecOk) &&
+          GF_IN_BOUNDS(gbase + (size_t)31 * F.in_f + 31 < (size_t)F.out_f * F.in_f);
+  return true;
+}
+
+// Stages the tile's row coordinates and its dL/d(delta) block, transposed to
+// s_gt[col][row], with plain loads (the caller synchronises afterwards).
+template <int NF, int GT>
+__device__ __forceinline__ void bwd32_stage_sync(const Params<NF>& p, const Bwd32Job& j, float* s_rows,
+                                                 float* s_gt) {
+  const DevField& F = p.f[j.fi];
+  const int th = j.th, tw = j.tw;
+  const int row0 = j.tr * 32, col0 = j.tc * 32;
   if (threadIdx.x < 32) s_rows[threadIdx.x] = (threadIdx.x < th) ? F.row[row0 + threadIdx.x] : 0.0f;
   // dL/d(delta) of the tile, transposed into s_gt[col][row]
   const size_t gbase = (size_t)row0 * F.in_f + col0;
-  if (th == 32 && tw == 32 && (F.bits & kFieldGradVecOk) &&
-      GF_IN_BOUNDS(gbase + (size_t)31 * F.in_f + 31 < (size_t)F.out_f * F.in_f)) {
+  if (j.vec) {
     if (GT == GF_F32) {
 #pragma unroll
-      for (int k = 0; k < 2; ++k) {  // 256 16-byte loads of 4 floats
+      for (int k = 0; k < (256 + 32 * kBwd32Warps - 1) / (32 * kBwd32Warps); ++k) {  // 256 16-byte loads of 4 floats
         const int q = threadIdx.x + k * (32 * kBwd32Warps);
         if (q < 256) {
           const int r = q >> 3, c = (q & 7) * 4;
@@ -1517,8 +1555,7 @@ __device__ __forceinline__ void bwd32_tile(const Params<NF>& p, int tg, int pair
         }
       }
     } else {
-      const int q = threadIdx.x;  // 128 16-byte loads of 8 bf16
-      if (q < 128) {
+      for (int q = threadIdx.x; q < 128; q += 32 * kBwd32Warps) {  // 128 16-byte loads of 8 bf16
         const int r = q >> 2, c = (q & 3) * 8;
         const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(F.grad) + gbase +
                                                         (size_t)r * F.in_f + c);
@@ -1540,7 +1577,18 @@ __device__ __forceinline__ void bwd32_tile(const Params<NF>& p, int tg, int pair
               : 0.0f;
     }
   }
-  __syncthreads();
+}
+
+// Sums pairs [lo, hi) of the tile (warp w takes lo + w, lo + w + kBwd32Warps,
+// ...) over its staged block and stores each pair's eight partial channels.
+template <int NF, bool NORM, bool CLAMP, int GT, bool EX2>
+__device__ __forceinline__ void bwd32_pairs(const Params<NF>& p, const Bwd32Job& j, int lo, int hi,
+                                            const float* s_rows, const float* s_gt, float* s_rt) {
+  const DevField& F = p.f[j.fi];
+  const int tr = j.tr, tc = j.tc, th = j.th, tw = j.tw;
+  const int64_t start = j.start, id_base = j.id_base;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int col0 = tc * 32;
   if (lo + warp >= hi) return;
   const bool cval = lane < tw;
   const float cc = cval ? F.col[col0 + lane] : 0.0f;
@@ -1593,7 +1641,16 @@ __device__ __forceinline__ void bwd32_tile(const Params<NF>& p, int tg, int pair
     const float a01 = __fmul_rn(h.y, dy);
     const float a11 = __fmul_rn(h.z, dy);
     const f2 H00 = pk2(h.x, h.x), H01 = pk2(h.y, h.y), A01 = pk2(a01, a01), A11 = pk2(a11, a11);
-    const f2 DY = pk2(dy, dy), MUR = pk2(a.x, a.x);
+    const f2 DY = pk2(dy, dy);
+    // the row terms of this pair, one row per lane, for the whole warp
+    __syncwarp();
+    {
+      const float dxl = __fsub_rn(s_rows[lane], a.x);
+      s_rt[lane] = dxl;
+      s_rt[32 + lane] = __fmul_rn(h.x, dxl);
+      s_rt[64 + lane] = __fmul_rn(h.y, dxl);
+    }
+    __syncwarp();
     bool track = false;
     // With the base-2 basis (tolerance-bound) a clamp at quad >= 64 is not
     // tracked: a clamped element's basis is below e^-32 = 1.3e-14 of the
@@ -1605,8 +1662,8 @@ __device__ __forceinline__ void bwd32_tile(const Params<NF>& p, int tg, int pair
     const f2 H11 = pk2(h.z, h.z);
     const float nf = fabsf(a.w);
     PairSums S = track
-                     ? bwd32_pair_rows<NORM, true, EX2>(s_rows, s_gcol, H00, H01, H11, A01, A11, DY, MUR, nclamp, nf)
-                     : bwd32_pair_rows<NORM, false, EX2>(s_rows, s_gcol, H00, H01, H11, A01, A11, DY, MUR, nclamp, nf);
+                     ? bwd32_pair_rows<NORM, true, EX2>(s_rt, s_gcol, H00, H01, H11, A01, A11, DY, nclamp, nf)
+                     : bwd32_pair_rows<NORM, false, EX2>(s_rt, s_gcol, H00, H01, H11, A01, A11, DY, nclamp, nf);
     float t0a, t0b, u0a, u0b, u1a, u1b, u2a, u2b, m0a, m0b, m1a, m1b;
     up2(S.T0, t0a, t0b);
     up2(S.U0, u0a, u0b);
@@ -1654,12 +1711,26 @@ __device__ __forceinline__ void bwd32_tile(const Params<NF>& p, int tg, int pair
   }
 }
 
+// One tile (or one chunk of a heavy tile's pairs), staged with plain loads.
+template <int NF, bool NORM, bool CLAMP, int GT, bool EX2>
+__device__ __forceinline__ void bwd32_tile(const Params<NF>& p, int tg, int pair_lo, int pair_hi, bool skip_heavy,
+                                           float* s_rows, float* s_gt, float* s_rt) {
+  Bwd32Job j;
+  if (!bwd32_job(p, tg, skip_heavy, j)) return;
+  const int lo = pair_lo, hi = min(pair_hi, j.count);
+  if (lo >= hi) return;
+  bwd32_stage_sync<NF, GT>(p, j, s_rows, s_gt);
+  __syncthreads();
+  bwd32_pairs<NF, NORM, CLAMP, GT, EX2>(p, j, lo, hi, s_rows, s_gt, s_rt + 96 * (threadIdx.x >> 5));
+}
+
 template <int NF, bool NORM, bool CLAMP, int GT, bool EX2>
 __global__ void __launch_bounds__(32 * kBwd32Warps)
 render_bwd32_kernel(const __grid_constant__ Params<NF> p) {
   __shared__ __align__(16) float s_rows[32];
   __shared__ __align__(16) float s_gt[32 * kGtStride];
-  bwd32_tile<NF, NORM, CLAMP, GT, EX2>(p, blockIdx.x, 0, INT32_MAX, true, s_rows, s_gt);
+  __shared__ __align__(16) float s_rt[kBwd32Warps * 96];
+  bwd32_tile<NF, NORM, CLAMP, GT, EX2>(p, blockIdx.x, 0, INT32_MAX, true, s_rows, s_gt, s_rt);
 }
 
 // Chunks of kHeavyChunk pairs of the heavy tiles (listed by bwd_prep), CTAs
@@ -1670,11 +1741,13 @@ __global__ void __launch_bounds__(32 * kBwd32Warps)
 render_bwd32_heavy_kernel(const __grid_constant__ Params<NF> p) {
   __shared__ __align__(16) float s_rows[32];
   __shared__ __align__(16) float s_gt[32 * kGtStride];
+  __shared__ __align__(16) float s_rt[kBwd32Warps * 96];
   const int n = min((int)*reinterpret_cast<volatile uint32_t*>(p.heavy_count), p.heavy_cap);
   const int2* items = reinterpret_cast<const int2*>(p.heavy);
   for (int i = blockIdx.x; i < n; i += gridDim.x) {
     const int2 it = items[i];
-    bwd32_tile<NF, NORM, CLAMP, GT, EX2>(p, it.x, it.y * kHeavyChunk, (it.y + 1) * kHeavyChunk, false, s_rows, s_gt);
+    bwd32_tile<NF, NORM, CLAMP, GT, EX2>(p, it.x, it.y * kHeavyChunk, (it.y + 1) * kHeavyChunk, false, s_rows, s_gt,
+                                         s_rt);
     __syncthreads();  // the next chunk restages the shared tile
   }
 }
@@ -2070,18 +2143,19 @@ gf_status run_forward(const gf_config* cfg, const gf_batch* batch, const Layout&
   return GF_OK;
 }
 
+template <int NF, bool N, bool C, int G, bool X>
+cudaError_t launch_bwd32(const Params<NF>& p, int grid, cudaStream_t st) {
+  const int hgrid = grid < kHeavyGridCap ? grid : kHeavyGridCap;
+  render_bwd32_kernel<NF, N, C, G, X><<<grid, 32 * kBwd32Warps, 0, st>>>(p);
+  render_bwd32_heavy_kernel<NF, N, C, G, X><<<hgrid, 32 * kBwd32Warps, 0, st>>>(p);
+  return cudaSuccess;
+}
+
 template <int NF, bool N, bool C, int G>
 cudaError_t launch_bwd_render(const Params<NF>& p, int grid, size_t smem, cudaStream_t st) {
   if (p.cfg.tile_out == 32 && p.cfg.tile_in == 32) {
-    const int hgrid = grid < kHeavyGridCap ? grid : kHeavyGridCap;
-    if (p.cfg.flags & GF_CFG_BWD_EXP2) {
-      render_bwd32_kernel<NF, N, C, G, true><<<grid, 32 * kBwd32Warps, 0, st>>>(p);
-      render_bwd32_heavy_kernel<NF, N, C, G, true><<<hgrid, 32 * kBwd32Warps, 0, st>>>(p);
-    } else {
-      render_bwd32_kernel<NF, N, C, G, false><<<grid, 32 * kBwd32Warps, 0, st>>>(p);
-      render_bwd32_heavy_kernel<NF, N, C, G, false><<<hgrid, 32 * kBwd32Warps, 0, st>>>(p);
-    }
-    return cudaSuccess;
+    if (p.cfg.flags & GF_CFG_BWD_EXP2) return launch_bwd32<NF, N, C, G, true>(p, grid, st);
+    return launch_bwd32<NF, N, C, G, false>(p, grid, st);
   }
   const cudaError_t e = allow_dynamic_smem<render_bwd_kernel<NF, N, C, G>>(kBwdSmemCapFloats * 4);
   if (e != cudaSuccess) return e;
