@@ -352,6 +352,51 @@ __global__ void __launch_bounds__(kGeoThreads) geometry_kernel(const __grid_cons
   }
 }
 
+// In-place inclusive prefix sums of `lines` lines of `len` ints each (line l,
+// element i at D[l * lstride + i * estride]) by the whole CTA.  When there are
+// fewer lines than threads, each line is cut into up to 32 segments summed by
+// separate threads (segment totals in s_seg, then one pass adding each
+// segment's offset), so a long line is not one thread's serial walk.
+// Integer sums: the result does not depend on the split.
+__device__ __forceinline__ void line_prefix(int* D, int lines, int len, int lstride, int estride, int* s_seg) {
+  const int tid = threadIdx.x, bs = blockDim.x;
+  int S = lines > 0 ? bs / lines : 1;
+  S = S < 1 ? 1 : (S > 32 ? 32 : S);
+  if (S > len) S = len > 0 ? len : 1;
+  const int seg = (len + S - 1) / S;
+  for (int w = tid; w < lines * S; w += bs) {
+    const int l = w / S, k = w % S;
+    const int i0 = k * seg, i1 = min(len, i0 + seg);
+    int* base = D + (size_t)l * lstride;
+    int acc = 0;
+    for (int i = i0; i < i1; ++i) {
+      acc += base[i * estride];
+      base[i * estride] = acc;
+    }
+    if (S > 1) s_seg[w] = acc;
+  }
+  __syncthreads();
+  if (S == 1) return;
+  for (int l = tid; l < lines; l += bs) {  // exclusive scan of each line's segment totals
+    int acc = 0;
+    for (int k = 0; k < S; ++k) {
+      const int v = s_seg[l * S + k];
+      s_seg[l * S + k] = acc;
+      acc += v;
+    }
+  }
+  __syncthreads();
+  for (int w = tid; w < lines * S; w += bs) {
+    const int l = w / S, k = w % S;
+    const int add = s_seg[w];
+    if (k == 0 || add == 0) continue;
+    const int i0 = k * seg, i1 = min(len, i0 + seg);
+    int* base = D + (size_t)l * lstride;
+    for (int i = i0; i < i1; ++i) base[i * estride] += add;
+  }
+  __syncthreads();
+}
+
 // ---------------------------------------------------------------------------
 // Forward kernel 1: stable binning counts, one CTA per field.
 //
@@ -368,6 +413,7 @@ __global__ void __launch_bounds__(kBinThreads)
 bin_kernel(const __grid_constant__ Params<NF> p, int smem_cap_ints) {
   extern __shared__ int s_dyn[];
   __shared__ int64_t s_warp[32];
+  __shared__ int s_seg[kBinThreads];
   __shared__ int s_last;
   const int fi = blockIdx.x;
   const DevField& F = p.f[fi];
@@ -384,16 +430,8 @@ bin_kernel(const __grid_constant__ Params<NF> p, int smem_cap_ints) {
     atomicAdd(&D[(b.y + 1) * W + b.w + 1], 1);
   }
   __syncthreads();
-  for (int r = tid; r < H; r += bs) {
-    int s = 0;
-    for (int c = 0; c < W; ++c) { s += D[r * W + c]; D[r * W + c] = s; }
-  }
-  __syncthreads();
-  for (int c = tid; c < W; c += bs) {
-    int s = 0;
-    for (int r = 0; r < H; ++r) { s += D[r * W + c]; D[r * W + c] = s; }
-  }
-  __syncthreads();
+  line_prefix(D, H, W, W, 1, s_seg);  // along each row
+  line_prefix(D, W, H, 1, W, s_seg);  // along each column
   const int T = F.ntr * F.ntc;
   const int per = (T + bs - 1) / bs;
   const int t0 = min(T, tid * per), t1 = min(T, t0 + per);
@@ -418,16 +456,26 @@ bin_kernel(const __grid_constant__ Params<NF> p, int smem_cap_ints) {
     __syncthreads();
     if (tid == 0) s_last = (atomicAdd(p.done, 1u) == gridDim.x - 1);
     __syncthreads();
-    if (s_last && tid == 0) {
+    if (s_last && tid < 32) {  // exclusive scan of the fields' pair counts, 32 at a time
       __threadfence();
       int64_t acc = 0;
-      for (int i = 0; i < p.n; ++i) {
-        p.pair_base[i] = acc;
-        acc += *((volatile int64_t*)&p.field_pairs[i]);
+      for (int i0 = 0; i0 < p.n; i0 += 32) {
+        const int i = i0 + tid;
+        const int64_t c = i < p.n ? *((volatile int64_t*)&p.field_pairs[i]) : 0;
+        int64_t x = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int64_t y = __shfl_up_sync(0xffffffffu, x, o);
+          if (tid >= o) x += y;
+        }
+        if (i < p.n) p.pair_base[i] = acc + x - c;
+        acc += __shfl_sync(0xffffffffu, x, 31);
       }
-      p.pair_base[p.n] = acc;
-      if (acc > p.batch_cap) atomicOr(p.status, GF_FLAG_CAPACITY);
-      *p.done = 0u;
+      if (tid == 0) {
+        p.pair_base[p.n] = acc;
+        if (acc > p.batch_cap) atomicOr(p.status, GF_FLAG_CAPACITY);
+        *p.done = 0u;
+      }
     }
   }
 }
@@ -495,9 +543,6 @@ __global__ void __launch_bounds__(32 * kEmitWarps) emit_pairs_kernel(const __gri
   }
 }
 
-struct WarpSync {
-  __device__ __forceinline__ void operator()() const { __syncwarp(); }
-};
 struct BlockSync {
   __device__ __forceinline__ void operator()() const { __syncthreads(); }
 };
@@ -548,46 +593,85 @@ __device__ __forceinline__ void scan_tile_list(const Params<NF>& p, const DevFie
   if (lane == 0 && found != L.count) atomicOr(p.status, GF_FLAG_INTERNAL);
 }
 
-// Forward kernel 1c: sort every tile list of at most kHeavyPairs ids, one
-// warp per tile, in shared memory (ids are < 2^31).  Longer lists are in the
-// heavy list and sorted by sort_heavy_kernel.
+// Bitonic sort of 32*R keys held by one warp, key i = v[i / 32] of lane
+// i % 32: partners closer than 32 apart are exchanged by shuffles, farther
+// ones sit in the same lane's registers.  Ascending.
+template <int R>
+__device__ __forceinline__ void warp_bitonic_sort(int32_t (&v)[R], int lane) {
+  constexpr int N = 32 * R;
+#pragma unroll
+  for (int k = 2; k <= N; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j >= 32) {
+        const int rj = j >> 5;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const int q = r ^ rj;
+          if (q > r) {
+            const bool up = ((r * 32 + lane) & k) == 0;
+            const int32_t lo = min(v[r], v[q]), hi = max(v[r], v[q]);
+            v[r] = up ? lo : hi;
+            v[q] = up ? hi : lo;
+          }
+        }
+      } else {
+        const bool lower = (lane & j) == 0;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const int32_t o = __shfl_xor_sync(0xffffffffu, v[r], j);
+          const bool up = ((r * 32 + lane) & k) == 0;
+          v[r] = (lower == up) ? min(v[r], o) : max(v[r], o);
+        }
+      }
+    }
+  }
+}
+
+// Loads a tile list of n <= 32*R ids into the warp's registers (padding with
+// INT32_MAX), sorts it unless it is already ascending, and writes it back.
+template <int R, int NF>
+__device__ __forceinline__ void sort_list_in_registers(const TileIds<NF>& L, int n, int lane) {
+  int32_t v[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) v[r] = (r * 32 + lane < n) ? (int32_t)L.ids[r * 32 + lane] : INT32_MAX;
+  bool descent = false;  // any key smaller than its predecessor
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    int32_t prev = __shfl_up_sync(0xffffffffu, v[r], 1);
+    if (r > 0) {
+      const int32_t last = __shfl_sync(0xffffffffu, v[r - 1], 31);
+      if (lane == 0) prev = last;
+    }
+    const int i = r * 32 + lane;
+    descent |= (i > 0 && i < n && prev > v[r]);
+  }
+  if (__ballot_sync(0xffffffffu, descent) == 0u) return;
+  warp_bitonic_sort<R>(v, lane);
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+    if (r * 32 + lane < n) L.ids[r * 32 + lane] = v[r];
+}
+
+// Forward kernel 1c: sort every tile list of at most kHeavyPairs ids
+// (ids are < 2^31), one warp per tile, in registers: 32, 64 or 128 keys by
+// the list's length.  Lists beyond kHeavyPairs ids are in the heavy list and
+// sorted by sort_heavy_kernel.
 constexpr int kSortWarps = 4;
+static_assert(kHeavyPairs <= 128, "sort_tiles_kernel sorts at most 128 ids in registers");
 
 template <int NF>
 __global__ void __launch_bounds__(32 * kSortWarps) sort_tiles_kernel(const __grid_constant__ Params<NF> p) {
-  __shared__ int32_t s_keys[kSortWarps][kHeavyPairs];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tg = blockIdx.x * kSortWarps + warp;
   if (tg >= p.total_tiles) return;  // whole warps
   const int fi = field_of_tile(p, tg);
   const TileIds<NF> L = tile_ids(p, fi, tg - p.f[fi].tile_base);
-  const int n0 = (int)L.count;
-  if (n0 <= 1 || n0 > kHeavyPairs || !L.complete()) return;
-  if (n0 <= 32) {
-    // one id per lane: leave a list that is already ascending alone, else a
-    // bitonic sort across the lanes (the sort network on register values)
-    int32_t v = lane < n0 ? (int32_t)L.ids[lane] : INT32_MAX;
-    const int32_t prev = __shfl_up_sync(0xffffffffu, v, 1);
-    if (__ballot_sync(0xffffffffu, lane > 0 && lane < n0 && prev > v) == 0u) return;
-#pragma unroll
-    for (int k = 2; k <= 32; k <<= 1) {
-#pragma unroll
-      for (int j = k >> 1; j > 0; j >>= 1) {
-        const int32_t o = __shfl_xor_sync(0xffffffffu, v, j);
-        const bool lower = (lane & j) == 0, up = (lane & k) == 0;
-        v = (lower == up) ? min(v, o) : max(v, o);
-      }
-    }
-    if (lane < n0) L.ids[lane] = v;
-    return;
-  }
-  int n = 64;
-  while (n < n0) n <<= 1;
-  int32_t* s = s_keys[warp];
-  for (int i = lane; i < n; i += 32) s[i] = i < n0 ? (int32_t)L.ids[i] : INT32_MAX;
-  __syncwarp();
-  bitonic_sort(s, n, lane, 32, WarpSync{});
-  for (int i = lane; i < n0; i += 32) L.ids[i] = s[i];
+  const int n = (int)L.count;
+  if (n <= 1 || n > kHeavyPairs || !L.complete()) return;
+  if (n <= 32) sort_list_in_registers<1>(L, n, lane);
+  else if (n <= 64) sort_list_in_registers<2>(L, n, lane);
+  else sort_list_in_registers<4>(L, n, lane);
 }
 
 // The heavy tiles' lists (more than kHeavyPairs ids): one CTA per tile,
