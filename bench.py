@@ -620,9 +620,10 @@ def time_single_field(f, fwd_exp2: bool, bwd_exp2: bool, out_dtype, steps: int, 
     _lib.check(L.gf_trace_events(None, 0))
     assert b.device_flags() == 0
     ms = start.elapsed_time(end) / steps
-    kern = {"render_fwd": 0.0, "render_bwd": 0.0}
+    kern = {"bin": 0.0, "render_fwd": 0.0, "render_bwd": 0.0}
     for s_ in range(steps):
         e = evs[7 * s_: 7 * s_ + 7]
+        kern["bin"] += e[0].elapsed_time(e[1]) / steps
         kern["render_fwd"] += e[1].elapsed_time(e[2]) / steps
         kern["render_bwd"] += e[4].elapsed_time(e[5]) / steps
     return ms, kern, evals
@@ -691,10 +692,12 @@ def time_dropin_train(f, steps: int, warmup: int):
 
 
 def dense_rows(a, ns_per_eval_fwd: float):
-    """Densified layers (1280x1280, K = 4096 and 16384): the per-tile candidate
-    scan reads all K boxes per tile, so its cost grows with K x tiles while the
-    render work grows with the pairs.  Each row compares the forward render
-    with that work at the whole-UNet rate per evaluation (the scan's excess)."""
+    """Densified layers (1280x1280, K = 4096 and 16384).  The BIN stage emits
+    and sorts (tile, id) pairs, so its cost follows the pair count, not K x
+    tiles: each row reports it beside the step (``bin_share``).  The forward
+    render is compared with its work at the whole-UNet rate per evaluation:
+    one field is 1600 tiles, a launch too small to fill the GPU the way the
+    91 k tiles of the UNet do (``small_launch_excess_share``)."""
     from guass_b200 import synthetic
 
     rows = {}
@@ -707,7 +710,8 @@ def dense_rows(a, ns_per_eval_fwd: float):
             "workload": f"1280x1280 field, K={k} (densified: log s ~ N(log(0.02*sqrt(1024/K)), 0.3)), bf16 delta",
             "ms_per_step": ms, "value": f.numel / (ms / 1e3), "unit": "elements/s", "evals": evals,
             "kernels_ms": kern, "render_fwd_at_unet_rate_ms": work_ms,
-            "scan_excess_share": max(0.0, kern["render_fwd"] - work_ms) / kern["render_fwd"],
+            "bin_share": kern["bin"] / ms,
+            "small_launch_excess_share": max(0.0, kern["render_fwd"] - work_ms) / kern["render_fwd"],
             "dropin_train": {"ms_per_step": t_ms, "peak_bytes": peak,
                              "k_times_tiles_bound_bytes": 40 * k * 1600,
                              "path": "cuda_field.gaussian_field_train + autograd backward, fp32 delta"}}
@@ -727,8 +731,8 @@ def single_field_configs(a, f_mhz, sm_count):
         ms, kern, evals = time_single_field(f, fx, bx, out_dtype, steps, a.warmup)
         ms_ref_basis, _, _ = time_single_field(f, False, False, out_dtype, steps, a.warmup)
         ref_ms = time_reference_cuda([f], out_dtype == torch.bfloat16, max(3, steps // 4), 2)
-        dom = max(kern, key=kern.get)
-        kind = "render_fwd" if dom == "render_fwd" else "render_bwd"
+        dom = max(("render_fwd", "render_bwd"), key=kern.get)
+        kind = dom
         out[name] = {
             "workload": f"{name}: {f.out_features}x{f.in_features} field, K={f.k}, {dt} delta, f32 dL/d(delta)",
             "value": f.numel / (ms / 1e3), "unit": "elements/s", "ms_per_step": ms, "evals": evals,

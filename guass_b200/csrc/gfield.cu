@@ -1906,12 +1906,15 @@ bwd_finalize_kernel(const __grid_constant__ Params<NF> p) {
 
 thread_local std::string g_last_error;
 
+// Process-wide: an autograd backward runs on its own thread, and its trace
+// events belong to the same step as the forward's.
 struct Trace {
   void* const* ev = nullptr;
   int n = 0;
   int used = 0;
 };
-thread_local Trace g_trace;
+Trace g_trace;
+std::mutex g_trace_mu;
 
 // NVTX range over the host-side enqueue of one stage ("gfield.<stage>"), so a
 // timeline profiler shows each entry point and kernel launch by name.  A
@@ -1924,6 +1927,7 @@ struct NvtxRange {
 };
 
 inline void trace_mark(cudaStream_t st) {
+  std::lock_guard<std::mutex> lock(g_trace_mu);
   if (g_trace.used < g_trace.n) {
     cudaEventRecord(reinterpret_cast<cudaEvent_t>(g_trace.ev[g_trace.used]), st);
     ++g_trace.used;
@@ -2385,13 +2389,17 @@ gf_status gf_workspace_status(void* workspace, gf_stream stream, int reset, uint
 
 gf_status gf_trace_events(void* const* events, int n) {
   if (n < 0 || (n > 0 && !events)) return gf::fail(GF_ERR_INVALID_ARG, "gf_trace_events: bad event array");
+  std::lock_guard<std::mutex> lock(gf::g_trace_mu);
   gf::g_trace.ev = events;
   gf::g_trace.n = n;
   gf::g_trace.used = 0;
   return GF_OK;
 }
 
-int gf_trace_count(void) { return gf::g_trace.used; }
+int gf_trace_count(void) {
+  std::lock_guard<std::mutex> lock(gf::g_trace_mu);
+  return gf::g_trace.used;
+}
 
 }  // extern "C"
 

@@ -186,8 +186,9 @@ gf_status gf_backward(const gf_config* cfg, const gf_batch* batch, void* workspa
 gf_status gf_workspace_status(void* workspace, gf_stream stream, int reset, uint32_t* flags_out);
 
 /* Profiling hook (no reference counterpart; the reference has no timing
- * facility).  After this call, gf_forward / gf_backward on the calling thread
- * record the caller's CUDA events (cudaEvent_t, passed as void*) on their
+ * facility).  After this call, gf_forward / gf_backward on any thread of the
+ * process (an autograd backward runs on its own thread) record the caller's
+ * CUDA events (cudaEvent_t, passed as void*) on their
  * stream: one before their first kernel and one after each kernel
  * (forward: 3 = start, bin, render; backward: 4 = start, prep, render,
  * finalize), consuming events[0..n) in order until all n are used.  n = 0

@@ -111,3 +111,32 @@ def test_checkpoint_fields_render_like_the_modules():
     assert cf.batch.device_flags() == 0
     for (name, m), w in zip(mods.items(), want):
         assert torch.equal(got[name], w)  # out_scale in the kernel == fp32 multiply after it
+
+
+def test_trace_events_cover_the_autograd_backward():
+    """gf_trace_events is process-wide: the batched render's backward, which
+    autograd runs on its own thread, records its four events after the
+    forward's three."""
+    import ctypes
+
+    from guass_b200 import _lib
+
+    mods = _modules()
+    bank = BatchedAdapters(mods, out_dtype=torch.float32, track_metadata=False)
+    bank.install()
+    L = _lib.lib()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+    for e in evs:
+        e.record()
+    torch.cuda.synchronize()
+    handles = (ctypes.c_void_p * 7)(*[e.cuda_event for e in evs])
+    _lib.check(L.gf_trace_events(handles, 7))
+    try:
+        loss = sum((d.float() ** 2).sum() for d in bank.render())
+        loss.backward()
+        torch.cuda.synchronize()
+        assert L.gf_trace_count() == 7
+    finally:
+        _lib.check(L.gf_trace_events(None, 0))
+    times = [evs[k].elapsed_time(evs[k + 1]) for k in range(6)]
+    assert all(t >= 0.0 for t in times)

@@ -3,8 +3,9 @@ tests/sweep_configs.py (the same seeds tests/test_oracle_sweep.py checks the
 oracle against the reference's own PyTorch path with): shapes 1..130, tile
 sizes 7..64, sigma multiplier 1.5..4.5, normalize on/off, clamp 20/80/none,
 isotropic and elongated Gaussians.  Binning bit-exact; fp32 delta within
-1e-5 rel plus an absolute floor of 2e-6 of the field's largest value;
-gradients within the condition-aware bound."""
+1e-5 rel plus an absolute floor of 2e-6 of the field's largest value
+against the oracle (host expf) and bit-identical to the reference's own
+extension on the same GPU; gradients within the condition-aware bound."""
 from __future__ import annotations
 
 import numpy as np
@@ -76,3 +77,26 @@ def test_gradients_no_farther_from_exact_than_reference_extension(ref_ext, seed)
     exact = exact_grads(f, tp, ids, **args)
     w_mine, w_ref = _worst_over_bound(mine, exact), _worst_over_bound(theirs, exact)
     assert w_mine <= max(w_ref, 0.1), f"seed {seed}: worst err/bound {w_mine:.3g} vs reference {w_ref:.3g}"
+
+
+@pytest.mark.parametrize("seed", range(24))
+def test_sweep_delta_bitwise_equal_to_reference_extension(ref_ext, seed):
+    """On every sweep configuration the fp32 delta is bit-identical to the
+    reference extension's on the same B200 (bins and ids equal too), outside
+    the edge tiles the reference leaves undefined (tests/ref_defects.py)."""
+    from ref_defects import reference_undefined_tiles, tile_mask_to_elements
+    from test_gpu_reference_ext import run_ref
+
+    f, kw = draw(seed)
+    args = dict(tile_out=kw["tile_out"], tile_in=kw["tile_in"], sigma=kw["sigma_multiplier"],
+                normalize=kw["normalize"], clamp=kw["clamp_quad"])
+    d_g, tp_g, ids_g, _ = run_ext(f, **args)
+    d_r, tp_r, ids_r, _ = run_ref(ref_ext, f, **args)
+    np.testing.assert_array_equal(tp_g, tp_r)
+    np.testing.assert_array_equal(ids_g, ids_r)
+    undefined = tile_mask_to_elements(
+        reference_undefined_tiles(f.out_features, f.in_features, args["tile_out"], args["tile_in"], tp_g),
+        f.out_features, f.in_features, args["tile_out"], args["tile_in"])
+    differ = d_g.view(np.uint32) != d_r.view(np.uint32)
+    assert not (differ & ~undefined).any(), \
+        f"seed {seed}: {int((differ & ~undefined).sum())} delta elements differ bitwise outside undefined tiles"
