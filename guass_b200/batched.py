@@ -288,17 +288,28 @@ class FieldBatch:
         self._backward_workspace()
         self._count_done = done
 
+    # The backward's pair partials take 32 bytes per pair of capacity.  Up to
+    # this size the workspace covers the whole id capacity and the backward is
+    # enqueued without waiting for the forward; beyond it, eager calls size it
+    # from the binning's pair count, which means waiting for that copy.
+    EAGER_WORKSPACE_BUDGET = 1 << 30
+
     def _backward_workspace(self) -> int:
         """Size the backward workspace; returns the pair capacity to pass.
-        Eager: the last binning's pair count (read when the copy is long
-        done); under capture: the id capacity (a replay may see any count)."""
+        For the whole id capacity when that fits EAGER_WORKSPACE_BUDGET (and
+        under capture, where a replay may see any count); otherwise, eagerly,
+        the last binning's pair count."""
         cap = self.ids.numel()
-        if self._count_done is not None and not torch.cuda.is_current_stream_capturing():
-            self._count_done.synchronize()
-            cap = max(1, min(cap, int(self._count_host[0])))
         self._batch.ids_capacity = cap
         need_b = self._lib.gf_workspace_bytes(ctypes.byref(self.cfg), ctypes.byref(self._batch),
                                               _lib.GF_PASS_BACKWARD)
+        if (need_b > self.EAGER_WORKSPACE_BUDGET and self._count_done is not None
+                and not torch.cuda.is_current_stream_capturing()):
+            self._count_done.synchronize()
+            cap = max(1, min(cap, int(self._count_host[0])))
+            self._batch.ids_capacity = cap
+            need_b = self._lib.gf_workspace_bytes(ctypes.byref(self.cfg), ctypes.byref(self._batch),
+                                                  _lib.GF_PASS_BACKWARD)
         self._batch.ids_capacity = self.ids.numel()
         if need_b == 0:
             raise RuntimeError("invalid batch: " + _lib.last_error())
