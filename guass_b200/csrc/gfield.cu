@@ -1458,7 +1458,11 @@ render_bwd_kernel(const __grid_constant__ Params<NF> p) {
 // floats so each lane's 128-bit read of four consecutive rows is aligned and
 // conflict free), next to the 32 row coordinates.  Lane = column; rows go in
 // pairs through packed fp32x2 arithmetic; the quadratic form is evaluated
-// exactly as in the forward.  The six per-pair channels are reduced across the warp with a
+// exactly as in the forward.  Per pair, the terms that depend on the row only
+// (dx and the reference-rounded products h00*dx, h01*dx) are computed once,
+// lane = row, into the warp's slice of shared memory and read back as
+// broadcasts.  Two warps per CTA: with ~14 pairs per tile, wider CTAs leave
+// warps idle at the tile's end.  The six per-pair channels are reduced across the warp with a
 // reduce-scatter (9 shuffles instead of 30); lanes 0, 4, ..., 28 then hold
 // channels 0..7 and write the pair's slot with one 32-byte store.
 //
