@@ -142,3 +142,34 @@ def test_reference_dq_rounding_is_the_contracted_form(ref_ext):
         agree += abs(c0 - c1) <= 3e-7 * abs(c0)
     assert checked >= 50
     assert agree == checked, f"{checked - agree} of {checked} single-element fields disagree"
+
+
+@pytest.mark.parametrize("cfg", ["cfg1", "cfg3slice"])
+def test_bf16_delta_equals_cast_of_reference_extension(ref_ext, cfg):
+    """The layer's bf16 delta (gaussian_linear.py:236 casts the extension's fp32
+    delta to the weight dtype) straight from the batched bf16 render with the
+    expf basis: bitwise equal to the reference extension's fp32 delta cast to
+    bf16 (round to nearest even) outside the reference's undefined tiles."""
+    from guass_b200.batched import FieldBatch, pack_fields
+
+    fields = [S.CONFIGS["cfg1"]()] if cfg == "cfg1" else S.cfg3()[::11]
+    shapes = [(f.out_features, f.in_features, f.k) for f in fields]
+    b = FieldBatch(shapes, out_dtype=torch.bfloat16)
+    mu, chol, amp, _ = pack_fields(fields, device="cuda")
+    while b.ensure_capacity(mu, chol, amp):
+        pass
+    mine = b.forward(mu, chol, amp).clone()
+    assert b.device_flags() == 0
+    off = 0
+    for f in fields:
+        d = f.to("cuda")
+        theirs, tp, _ = ref_ext.gaussian_field_forward(d.row_coords, d.col_coords, d.mu, d.chol_raw, d.amp,
+                                                       32, 32, 3.0, False, 80.0)
+        want = theirs.to(torch.bfloat16).view(torch.int16).cpu().numpy()
+        got = mine[off:off + f.numel].view(torch.int16).cpu().numpy()
+        off += f.numel
+        undefined = tile_mask_to_elements(
+            reference_undefined_tiles(f.out_features, f.in_features, 32, 32, tp.cpu().numpy()),
+            f.out_features, f.in_features, 32, 32)
+        differ = got != want
+        assert not (differ & ~undefined).any(), f"{f.name}: {int((differ & ~undefined).sum())} bf16 elements differ"
